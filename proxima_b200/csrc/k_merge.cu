@@ -1,0 +1,177 @@
+// Merges of sorted top-k lists and the conversion to caller outputs.
+//
+// The reference keeps one heap per query and converts its sorted contents to
+// natural distances with -1 / f32::MAX / f32::MIN padding
+// (crates/core/src/flat.rs:139-147, pq.rs:332-346). Here the per-CTA (or
+// per-GPU) sorted lists are merged on the device and converted in one pass.
+#include "px_common.cuh"
+#include "px_kernels.h"
+
+namespace px {
+
+namespace {
+
+constexpr int kMergeWarps = 4;
+
+// One warp per query: a k-step tournament over `nlists` sorted lists. Each
+// lane owns lists lane, lane+32, ...; it caches the smallest of its heads and
+// rescans only after its own list advanced.
+__global__ void __launch_bounds__(kMergeWarps * 32)
+merge_lists_kernel(const uint64_t* __restrict__ lists, int64_t nq, int nlists, int list_len,
+                   int k, uint64_t* __restrict__ out) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t* heads = reinterpret_cast<uint64_t*>(smem_raw) + static_cast<size_t>(warp) * nlists;
+  int* pos = reinterpret_cast<int*>(reinterpret_cast<uint64_t*>(smem_raw) +
+                                    static_cast<size_t>(kMergeWarps) * nlists) +
+             static_cast<size_t>(warp) * nlists;
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * kMergeWarps + warp;
+  if (q >= nq) return;
+  const uint64_t* ql = lists + q * static_cast<int64_t>(nlists) * list_len;
+
+  uint64_t best = PX_EMPTY;
+  int best_list = -1;
+  for (int l = lane; l < nlists; l += 32) {
+    uint64_t h = list_len > 0 ? ql[static_cast<int64_t>(l) * list_len] : PX_EMPTY;
+    heads[l] = h;
+    pos[l] = 0;
+    if (h < best) {
+      best = h;
+      best_list = l;
+    }
+  }
+  __syncwarp();
+  for (int j = 0; j < k; ++j) {
+    uint64_t v = best;
+    int src = lane;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      uint64_t ov = __shfl_xor_sync(0xffffffffu, v, off);
+      int os = __shfl_xor_sync(0xffffffffu, src, off);
+      if (ov < v || (ov == v && os < src)) {
+        v = ov;
+        src = os;
+      }
+    }
+    if (lane == 0) out[q * k + j] = v;
+    if (v == PX_EMPTY) {
+      for (int jj = j + 1 + lane; jj < k; jj += 32) out[q * k + jj] = PX_EMPTY;
+      return;
+    }
+    if (lane == src) {
+      int l = best_list;
+      int p = ++pos[l];
+      heads[l] = p < list_len ? ql[static_cast<int64_t>(l) * list_len + p] : PX_EMPTY;
+      best = PX_EMPTY;
+      best_list = -1;
+      for (int ll = lane; ll < nlists; ll += 32) {
+        uint64_t h = heads[ll];
+        if (h < best) {
+          best = h;
+          best_list = ll;
+        }
+      }
+    }
+    __syncwarp();
+  }
+}
+
+__device__ __forceinline__ int64_t map_row(uint32_t row, const IdSegments& s) {
+  int lo = 0, hi = s.nseg - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (s.local_begin[mid] <= static_cast<int64_t>(row)) lo = mid; else hi = mid - 1;
+  }
+  return s.global_begin[lo] + (static_cast<int64_t>(row) - s.local_begin[lo]) + s.id_offset;
+}
+
+__global__ void emit_kernel(const uint64_t* __restrict__ cands, int64_t total, bool l2, bool natural,
+                            IdSegments segs, int64_t* __restrict__ out_ids,
+                            float* __restrict__ out_dists) {
+  int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  uint64_t c = cands[i];
+  if (c == PX_EMPTY) {
+    out_ids[i] = -1;
+    out_dists[i] = natural ? pad_dist(l2) : 3.40282347e+38f;
+  } else {
+    out_ids[i] = map_row(cand_row(c), segs);
+    float key = cand_key(c);
+    out_dists[i] = natural ? natural_dist(key, l2) : key;
+  }
+}
+
+// One thread per query: G-way merge of per-shard sorted (key, id) lists.
+__global__ void merge_shards_kernel(const float* __restrict__ keys, const int64_t* __restrict__ ids,
+                                    int nshard, int64_t nq, int k, bool l2, bool natural,
+                                    float* __restrict__ out_dists, int64_t* __restrict__ out_ids) {
+  int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  int pos[8];
+  for (int g = 0; g < nshard; ++g) pos[g] = 0;
+  const int64_t stride = nq * k;
+  for (int j = 0; j < k; ++j) {
+    int win = -1;
+    uint32_t wk = 0;
+    int64_t wid = 0;
+    for (int g = 0; g < nshard; ++g) {
+      if (pos[g] >= k) continue;
+      int64_t e = g * stride + q * k + pos[g];
+      int64_t id = ids[e];
+      if (id < 0) continue;
+      uint32_t o = key_to_ord(keys[e]);
+      if (win < 0 || o < wk || (o == wk && id < wid)) {
+        win = g;
+        wk = o;
+        wid = id;
+      }
+    }
+    if (win < 0) {
+      out_ids[q * k + j] = -1;
+      out_dists[q * k + j] = natural ? pad_dist(l2) : 3.40282347e+38f;
+    } else {
+      ++pos[win];
+      float key = ord_to_key(wk);
+      out_ids[q * k + j] = wid;
+      out_dists[q * k + j] = natural ? natural_dist(key, l2) : key;
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_merge_lists(const uint64_t* lists, int64_t nq, int nlists, int list_len, int k,
+                               uint64_t* out, cudaStream_t stream) {
+  if (nq == 0 || k == 0) return cudaSuccess;
+  const size_t smem = static_cast<size_t>(kMergeWarps) * nlists * (sizeof(uint64_t) + sizeof(int));
+  cudaError_t e = cudaFuncSetAttribute(merge_lists_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  const int64_t blocks = (nq + kMergeWarps - 1) / kMergeWarps;
+  merge_lists_kernel<<<static_cast<unsigned>(blocks), kMergeWarps * 32, smem, stream>>>(
+      lists, nq, nlists, list_len, k, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_emit(const uint64_t* cands, int64_t nq, int k, bool l2, bool natural,
+                        IdSegments segs, int64_t* out_ids, float* out_dists, cudaStream_t stream) {
+  const int64_t total = nq * k;
+  if (total == 0) return cudaSuccess;
+  const int threads = 256;
+  emit_kernel<<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0, stream>>>(
+      cands, total, l2, natural, segs, out_ids, out_dists);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_merge_shards(const float* keys, const int64_t* ids, int nshard, int64_t nq, int k,
+                                bool l2, bool natural, float* out_dists, int64_t* out_ids,
+                                cudaStream_t stream) {
+  if (nq == 0 || k == 0) return cudaSuccess;
+  if (nshard < 1 || nshard > 8) return cudaErrorInvalidValue;
+  const int threads = 128;
+  merge_shards_kernel<<<static_cast<unsigned>((nq + threads - 1) / threads), threads, 0, stream>>>(
+      keys, ids, nshard, nq, k, l2, natural, out_dists, out_ids);
+  return cudaGetLastError();
+}
+
+}  // namespace px

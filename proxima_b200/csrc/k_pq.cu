@@ -1,0 +1,207 @@
+// PQ asymmetric-distance scan (K3 LUT build, K4 scan) and the nearest-centroid
+// kernel used by PQ encoding and k-means assignment.
+//
+// Arithmetic restated from crates/core/src/pq.rs:
+//   adc_table  (pq.rs:123-136): table[sub*ksub + c] = l2_sqr(q_sub, centroid)
+//                               or -inner_product, exact 8-lane order;
+//   scan       (pq.rs:314-323): key = 0.0; key += table[sub*ksub + code[sub]]
+//                               for sub = 0..m-1, sequential f32 adds;
+//   encode_into(pq.rs:107-121) and the kmeans assignment (pq.rs:155-167):
+//                               argmin over centroids with strict '<', so the
+//                               first of equal distances wins.
+// All three are bit-exact with the CPU.
+#include "px_common.cuh"
+#include "px_kernels.h"
+
+namespace px {
+
+namespace {
+
+constexpr int kPqThreads = 256;
+constexpr int kPqRowsPerIter = 256;
+
+__global__ void pq_lut_kernel(const float* __restrict__ books, int m, int ksub, int dsub, bool l2,
+                              const float* __restrict__ queries, float* __restrict__ lut) {
+  const int q = blockIdx.x;
+  const int dim = m * dsub;
+  const float* qv = queries + static_cast<int64_t>(q) * dim;
+  float* out = lut + static_cast<int64_t>(q) * m * ksub;
+  for (int i = threadIdx.x; i < m * ksub; i += blockDim.x) {
+    const int sub = i / ksub;
+    const float* cen = books + static_cast<int64_t>(i) * dsub;
+    const float* qs = qv + sub * dsub;
+    out[i] = l2 ? exact_key<true>(qs, cen, dsub) : exact_key<false>(qs, cen, dsub);
+  }
+}
+
+// One CTA scans `rows_per_cta` codes for G queries. Shared-memory LUT layout
+// is [sub][code][G]: the G threads that share a code read G consecutive words,
+// so a warp's gathers touch at most 32/G distinct 32-word rows.
+template <int G, int BUF>
+__global__ void __launch_bounds__(kPqThreads)
+pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
+               const float* __restrict__ lut, int nq, int k, int64_t rows_per_cta,
+               const uint8_t* __restrict__ mask, uint64_t* __restrict__ partial) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint64_t* s_buf = reinterpret_cast<uint64_t*>(smem_raw);
+  uint64_t* s_thr = s_buf + G * BUF;  // G words, padded to an even count
+  int* s_cnt = reinterpret_cast<int*>(s_thr + ((G + 1) & ~1));
+  float* s_lut = reinterpret_cast<float*>(s_cnt + ((G + 3) & ~3));
+
+  const int tid = threadIdx.x;
+  const int q0 = blockIdx.y * G;
+  const int gcount = min(G, nq - q0);
+  const int table = m * ksub;
+
+  BlockTopK<G, BUF> topk;
+  topk.init(s_buf, s_cnt, s_thr, tid, kPqThreads);
+  for (int i = tid; i < G * table; i += kPqThreads) {
+    const int e = i / G, g = i - e * G;
+    s_lut[i] = g < gcount ? lut[static_cast<int64_t>(q0 + g) * table + e] : 0.f;
+  }
+  __syncthreads();
+
+  const int g = tid % G;
+  const int slot = tid / G;               // 0 .. 256/G - 1
+  constexpr int kSlots = kPqThreads / G;  // codes per step
+  const int64_t row_begin = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
+  const int64_t row_end = min(n, row_begin + rows_per_cta);
+  const bool vec16 = (m & 15) == 0;
+  uint64_t thr = PX_EMPTY;
+
+  for (int64_t it = row_begin; it < row_end; it += kPqRowsPerIter) {
+#pragma unroll 1
+    for (int step = 0; step < G; ++step) {
+      const int64_t r = it + step * kSlots + slot;
+      if (r < row_end && g < gcount && (mask == nullptr || mask[r] != 0)) {
+        const uint8_t* code = codes + r * m;
+        float key = 0.0f;
+        if (vec16) {
+          for (int b = 0; b < m; b += 16) {
+            const uint4 w = __ldg(reinterpret_cast<const uint4*>(code + b));
+            const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+#pragma unroll
+              for (int bi = 0; bi < 4; ++bi) {
+                const int sub = b + wi * 4 + bi;
+                const uint32_t c = (words[wi] >> (8 * bi)) & 0xFFu;
+                key = __fadd_rn(key, s_lut[(sub * ksub + c) * G + g]);
+              }
+            }
+          }
+        } else {
+          for (int sub = 0; sub < m; ++sub) {
+            const uint32_t c = code[sub];
+            key = __fadd_rn(key, s_lut[(sub * ksub + c) * G + g]);
+          }
+        }
+        topk.offer(g, pack_cand(key, static_cast<uint32_t>(r)), thr);
+      }
+    }
+    __syncthreads();
+    topk.maybe_compact(k, kPqRowsPerIter, tid, kPqThreads);
+    thr = s_thr[g];
+  }
+
+  __syncthreads();
+  topk.compact_all(k, tid, kPqThreads);
+  const int ncta = gridDim.x;
+  for (int i = tid; i < gcount * k; i += kPqThreads) {
+    const int gg = i / k, j = i - gg * k;
+    partial[(static_cast<int64_t>(q0 + gg) * ncta + blockIdx.x) * k + j] = s_buf[gg * BUF + j];
+  }
+}
+
+template <int G, int BUF>
+cudaError_t launch_pq_g(const PqScanArgs& a, cudaStream_t stream) {
+  const size_t smem = pq_smem_for(G, a.m, a.ksub, a.k);
+  auto kern = pq_scan_kernel<G, BUF>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(a.ncta, (a.nq + G - 1) / G);
+  kern<<<grid, kPqThreads, smem, stream>>>(a.codes, a.n, a.m, a.ksub, a.lut, a.nq, a.k,
+                                           a.rows_per_cta, a.mask, a.partial);
+  return cudaGetLastError();
+}
+
+template <int BUF>
+cudaError_t launch_pq_buf(const PqScanArgs& a, cudaStream_t stream) {
+  switch (a.group) {
+    case 1: return launch_pq_g<1, BUF>(a, stream);
+    case 2: return launch_pq_g<2, BUF>(a, stream);
+    case 4: return launch_pq_g<4, BUF>(a, stream);
+    default: return launch_pq_g<8, BUF>(a, stream);
+  }
+}
+
+int pq_buf_for(int k) {
+  if (k + kPqRowsPerIter <= 512) return 512;
+  return 1024;
+}
+
+// Nearest centroid: grid.y = subspace, one thread per vector. All threads of
+// a warp walk the same centroids, so centroid reads are broadcasts.
+__global__ void nearest_centroid_kernel(const float* __restrict__ vectors, int64_t n, int m,
+                                        int dsub, int ksub, const float* __restrict__ books,
+                                        uint32_t* __restrict__ out_assign,
+                                        uint8_t* __restrict__ out_codes) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int sub = blockIdx.y;
+  if (i >= n) return;
+  const float* v = vectors + i * static_cast<int64_t>(m) * dsub + sub * dsub;
+  const float* book = books + static_cast<int64_t>(sub) * ksub * dsub;
+  uint32_t best = 0;
+  float best_d = 3.40282347e+38f;
+  for (int c = 0; c < ksub; ++c) {
+    const float dist = exact_dot_or_l2<true>(v, book + static_cast<int64_t>(c) * dsub, dsub);
+    if (dist < best_d) {
+      best_d = dist;
+      best = static_cast<uint32_t>(c);
+    }
+  }
+  if (out_assign) out_assign[i * m + sub] = best;
+  if (out_codes) out_codes[i * m + sub] = static_cast<uint8_t>(best);
+}
+
+}  // namespace
+
+int pq_max_k() { return 1024 - kPqRowsPerIter; }
+
+size_t pq_smem_for(int group, int m, int ksub, int k) {
+  const int buf = pq_buf_for(k);
+  return sizeof(uint64_t) * (group * buf + ((group + 1) & ~1)) + sizeof(int) * ((group + 3) & ~3) +
+         sizeof(float) * static_cast<size_t>(group) * m * ksub;
+}
+
+int pq_group_for(int m, int ksub, int64_t nq) {
+  const size_t lut_budget = 160 * 1024;
+  int g = 8;
+  while (g > 1 && (static_cast<size_t>(g) * m * ksub * sizeof(float) > lut_budget || g / 2 >= nq)) g >>= 1;
+  return g;
+}
+
+cudaError_t launch_pq_lut(const float* books, int m, int ksub, int dsub, bool l2,
+                          const float* queries, int nq, float* lut, cudaStream_t stream) {
+  if (nq == 0) return cudaSuccess;
+  pq_lut_kernel<<<nq, 256, 0, stream>>>(books, m, ksub, dsub, l2, queries, lut);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pq_scan(const PqScanArgs& a, cudaStream_t stream) {
+  if (pq_buf_for(a.k) == 512) return launch_pq_buf<512>(a, stream);
+  return launch_pq_buf<1024>(a, stream);
+}
+
+cudaError_t launch_nearest_centroid(const float* vectors, int64_t n, int m, int dsub, int ksub,
+                                    const float* books, uint32_t* out_assign, uint8_t* out_codes,
+                                    cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  const int threads = 128;
+  dim3 grid(static_cast<unsigned>((n + threads - 1) / threads), m);
+  nearest_centroid_kernel<<<grid, threads, 0, stream>>>(vectors, n, m, dsub, ksub, books,
+                                                        out_assign, out_codes);
+  return cudaGetLastError();
+}
+
+}  // namespace px

@@ -1,0 +1,94 @@
+// Shard and query preparation for the tensor-core path.
+//
+// The fp32 rows are kept as given (the exact rescoring and the streaming scan
+// read them); beside them each row is split for the 3xTF32 contraction:
+//   hi = tf32_rn(x),  lo = tf32_rn(x - hi)      (x - hi is exact in fp32)
+// so that q.x ~= qhi.xhi + qhi.xlo + qlo.xhi with an error of a few 2^-22
+// relative per product. Rows are padded with zeros to a multiple of 32
+// floats, which leaves every dot product unchanged. `norms` holds the squared
+// L2 norm of each row for the approximate key ||x||^2 - 2 q.x.
+#include "px_common.cuh"
+#include "px_kernels.h"
+
+namespace px {
+
+namespace {
+
+__device__ __forceinline__ float tf32_rn(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// One warp per row.
+__global__ void prepare_rows_kernel(const float* __restrict__ src, int64_t n, int d, int ld,
+                                    float* __restrict__ dst, float* __restrict__ hi,
+                                    float* __restrict__ lo, float* __restrict__ norms,
+                                    int* __restrict__ lo_nonzero) {
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= n) return;
+  bool nz = false;
+  for (int e = lane; e < ld; e += 32) {
+    float x = e < d ? src[row * d + e] : 0.f;
+    if (dst) dst[row * ld + e] = x;
+    if (hi) {
+      float h = tf32_rn(x);
+      float l = tf32_rn(__fsub_rn(x, h));
+      hi[row * ld + e] = h;
+      if (lo) lo[row * ld + e] = l;
+      nz |= (l != 0.f);
+    }
+  }
+  __syncwarp();
+  const bool any_nz = __any_sync(0xffffffffu, nz);
+  if (lo_nonzero && any_nz && lane == 0) atomicOr(lo_nonzero, 1);
+  if (norms && lane == 0) {
+    // Squared norm in the reference's 8-lane order (l2_sqr(x, 0)).
+    const float* x = (dst ? dst + row * ld : src + row * d);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const int chunks = d >> 3;
+    for (int c = 0; c < chunks; ++c)
+#pragma unroll
+      for (int l = 0; l < 8; ++l) acc[l] = __fadd_rn(acc[l], __fmul_rn(x[c * 8 + l], x[c * 8 + l]));
+    float s = acc[0];
+#pragma unroll
+    for (int l = 1; l < 8; ++l) s = __fadd_rn(s, acc[l]);
+    for (int i = chunks * 8; i < d; ++i) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
+    norms[row] = s;
+  }
+}
+
+__global__ void zero_rows_kernel(float* __restrict__ p, int64_t begin, int64_t end, int ld) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x + begin * ld;
+  if (i < end * ld) p[i] = 0.f;
+}
+
+}  // namespace
+
+cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, float* dst, float* hi,
+                                float* lo, float* norms, int* lo_nonzero, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t blocks = (n * 32 + threads - 1) / threads;
+  prepare_rows_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(src, n, d, ld, dst, hi,
+                                                                          lo, norms, lo_nonzero);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_split_queries(const float* q, int64_t nq, int d, int ld, int64_t rows_alloc,
+                                 float* hi, float* lo, float* norms, int* lo_nonzero,
+                                 cudaStream_t stream) {
+  cudaError_t e = launch_prepare_rows(q, nq, d, ld, nullptr, hi, lo, norms, lo_nonzero, stream);
+  if (e != cudaSuccess) return e;
+  if (rows_alloc > nq) {
+    const int64_t count = (rows_alloc - nq) * ld;
+    const int threads = 256;
+    const unsigned blocks = static_cast<unsigned>((count + threads - 1) / threads);
+    zero_rows_kernel<<<blocks, threads, 0, stream>>>(hi, nq, rows_alloc, ld);
+    if (lo) zero_rows_kernel<<<blocks, threads, 0, stream>>>(lo, nq, rows_alloc, ld);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace px

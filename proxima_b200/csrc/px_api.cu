@@ -1,0 +1,607 @@
+// Host runtime and C ABI of libproxima_b200 (declared in include/px.h).
+//
+// A handle owns one shard per device: the rows it holds (fp32, plus the tf32
+// split planes and squared norms the tensor-core path reads), a stream, and
+// grow-only workspaces, so a warmed-up search performs no device allocation.
+// Searches run every shard on its own device and stream, gather the per-shard
+// sorted top-k lists on the first device and merge them there (ties on the
+// key go to the smaller global id).
+//
+// Validation and messages restate the reference's checks
+// (crates/core/src/flat.rs:72-85, 106-123, 150-172; pq.rs:54-72, 266-309,
+// 361-377; crates/py/src/lib.rs) as status codes instead of panics.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/px.h"
+#include "px_common.cuh"
+#include "px_kernels.h"
+#include "px_runtime.h"
+
+using namespace px;
+
+namespace px {
+
+thread_local std::string g_last_error;
+
+px_status set_error(px_status s, const std::string& msg) {
+  g_last_error = msg;
+  return s;
+}
+
+px_status cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return PX_OK;
+  return set_error(e == cudaErrorMemoryAllocation ? PX_ENOMEM : PX_ECUDA,
+                   std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+DeviceGuard::DeviceGuard(int dev) {
+  if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+  cudaSetDevice(dev);
+}
+DeviceGuard::~DeviceGuard() {
+  if (prev >= 0) cudaSetDevice(prev);
+}
+
+cudaError_t DevBuf::reserve(size_t need) {
+  if (need <= bytes) return cudaSuccess;
+  release();
+  cudaError_t e = cudaMalloc(&ptr, need);
+  if (e != cudaSuccess) {
+    ptr = nullptr;
+    cudaGetLastError();
+    return e;
+  }
+  bytes = need;
+  return cudaSuccess;
+}
+
+void DevBuf::release() {
+  if (ptr) cudaFree(ptr);
+  ptr = nullptr;
+  bytes = 0;
+}
+
+// Carves 256-byte aligned sub-buffers out of one reserved block.
+void* Carver::take(size_t bytes) {
+  size_t off = (used + 255) & ~size_t(255);
+  used = off + bytes;
+  return base ? static_cast<char*>(base) + off : nullptr;
+}
+
+bool all_finite(const float* p, int64_t count) {
+  for (int64_t i = 0; i < count; ++i)
+    if (!std::isfinite(p[i])) return false;
+  return true;
+}
+
+int device_sm_count(int dev) {
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    sms = 148;
+  return sms;
+}
+
+px_status resolve_devices(const int32_t* devices, int32_t ndev, std::vector<int>& out) {
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return set_error(PX_ECUDA, std::string("no CUDA device available: ") +
+                                   (e == cudaSuccess ? "device count is 0" : cudaGetErrorString(e)));
+  }
+  out.clear();
+  if (devices == nullptr || ndev <= 0) {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    out.push_back(cur);
+    return PX_OK;
+  }
+  if (ndev > 8) return set_error(PX_EINVAL, "at most 8 devices per handle");
+  for (int i = 0; i < ndev; ++i) {
+    if (devices[i] < 0 || devices[i] >= count)
+      return set_error(PX_EINVAL, "device ordinal " + std::to_string(devices[i]) +
+                                      " out of range (visible devices: " + std::to_string(count) + ")");
+    for (int j = 0; j < i; ++j)
+      if (devices[j] == devices[i]) return set_error(PX_EINVAL, "duplicate device ordinal");
+    out.push_back(devices[i]);
+  }
+  return PX_OK;
+}
+
+// Splits n rows into `parts` contiguous runs (remainder spread over the first).
+void split_rows(int64_t n, int parts, std::vector<int64_t>& begin, std::vector<int64_t>& count) {
+  begin.resize(parts);
+  count.resize(parts);
+  int64_t base = n / parts, rem = n % parts, at = 0;
+  for (int p = 0; p < parts; ++p) {
+    count[p] = base + (p < rem ? 1 : 0);
+    begin[p] = at;
+    at += count[p];
+  }
+}
+
+px_status Segments::sync_device() {
+  if (!dirty) return PX_OK;
+  const size_t need = sizeof(int64_t) * 2 * std::max<size_t>(1, local.size());
+  cudaError_t e = dev.reserve(need);
+  if (e != cudaSuccess) return cuda_status(e, "segment table allocation");
+  std::vector<int64_t> host(2 * std::max<size_t>(1, local.size()), 0);
+  for (size_t i = 0; i < local.size(); ++i) {
+    host[i] = local[i];
+    host[local.size() + i] = global[i];
+  }
+  e = cudaMemcpy(dev.ptr, host.data(), sizeof(int64_t) * host.size(), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_status(e, "segment table upload");
+  dirty = false;
+  return PX_OK;
+}
+
+IdSegments Segments::view(int64_t id_offset) const {
+  IdSegments s;
+  const size_t ns = std::max<size_t>(1, local.size());
+  s.local_begin = static_cast<const int64_t*>(dev.ptr);
+  s.global_begin = static_cast<const int64_t*>(dev.ptr) + ns;
+  s.nseg = static_cast<int>(local.empty() ? 1 : local.size());
+  s.id_offset = id_offset;
+  return s;
+}
+
+// Builds the shard-local mask from a global one through the segment table.
+void Segments::local_mask(const uint8_t* global_mask, int64_t n_local, std::vector<uint8_t>& out) const {
+  out.assign(static_cast<size_t>(n_local), 0);
+  for (size_t i = 0; i < local.size(); ++i) {
+    int64_t end = (i + 1 < local.size()) ? local[i + 1] : n_local;
+    std::memcpy(out.data() + local[i], global_mask + global[i], static_cast<size_t>(end - local[i]));
+  }
+}
+
+}  // namespace px
+
+// ===========================================================================
+// FlatIndex
+// ===========================================================================
+
+px_status FlatShard::ensure_capacity(int64_t need, int ld) {
+  if (need <= cap) return PX_OK;
+  int64_t new_cap = std::max<int64_t>(need, cap + cap / 2);
+  const size_t row_bytes = sizeof(float) * ld;
+  const size_t plane_bytes = static_cast<size_t>(new_cap) * row_bytes;
+  size_t free_b = 0, total_b = 0;
+  if (cudaMemGetInfo(&free_b, &total_b) == cudaSuccess) {
+    const size_t need_b = plane_bytes * 3 + sizeof(float) * new_cap;
+    if (need_b > free_b && new_cap > need) {
+      new_cap = need;  // drop the growth slack before giving up
+    }
+  }
+  float *nx = nullptr, *nhi = nullptr, *nlo = nullptr, *nn = nullptr;
+  const size_t pb = static_cast<size_t>(new_cap) * row_bytes;
+  cudaError_t e = cudaMalloc(&nx, pb);
+  if (e == cudaSuccess) e = cudaMalloc(&nhi, pb);
+  if (e == cudaSuccess) e = cudaMalloc(&nlo, pb);
+  if (e == cudaSuccess) e = cudaMalloc(&nn, sizeof(float) * new_cap);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    if (nx) cudaFree(nx);
+    if (nhi) cudaFree(nhi);
+    if (nlo) cudaFree(nlo);
+    if (nn) cudaFree(nn);
+    return set_error(PX_ENOMEM, "device allocation of " + std::to_string(new_cap) +
+                                    " rows failed on device " + std::to_string(device) + ": " +
+                                    cudaGetErrorString(e));
+  }
+  if (n > 0) {
+    const size_t used = static_cast<size_t>(n) * row_bytes;
+    cudaMemcpyAsync(nx, x, used, cudaMemcpyDeviceToDevice, stream);
+    cudaMemcpyAsync(nhi, hi, used, cudaMemcpyDeviceToDevice, stream);
+    cudaMemcpyAsync(nlo, lo, used, cudaMemcpyDeviceToDevice, stream);
+    cudaMemcpyAsync(nn, norms, sizeof(float) * n, cudaMemcpyDeviceToDevice, stream);
+    cudaStreamSynchronize(stream);
+  }
+  if (x) cudaFree(x);
+  if (hi) cudaFree(hi);
+  if (lo) cudaFree(lo);
+  if (norms) cudaFree(norms);
+  x = nx;
+  hi = nhi;
+  lo = nlo;
+  norms = nn;
+  cap = new_cap;
+  return PX_OK;
+}
+
+void FlatShard::release() {
+  DeviceGuard g(device);
+  if (stream) cudaStreamSynchronize(stream);
+  if (x) cudaFree(x);
+  if (hi) cudaFree(hi);
+  if (lo) cudaFree(lo);
+  if (norms) cudaFree(norms);
+  x = hi = lo = norms = nullptr;
+  if (flag) cudaFree(flag);
+  flag = nullptr;
+  ws.release();
+  stage.release();
+  segs.dev.release();
+  if (stream) cudaStreamDestroy(stream);
+  stream = nullptr;
+}
+
+// Appends rows that are already on this shard's device.
+px_status FlatShard::append_device(const float* d_src, int64_t count, int d, int ld,
+                                   int64_t global_begin) {
+  px_status s = ensure_capacity(n + count, ld);
+  if (s != PX_OK) return s;
+  cudaError_t e = launch_prepare_rows(d_src, count, d, ld, x + n * ld, hi + n * ld, lo + n * ld,
+                                      norms + n, flag, stream);
+  if (e != cudaSuccess) return cuda_status(e, "prepare_rows launch");
+  segs.local.push_back(n);
+  segs.global.push_back(global_begin);
+  segs.dirty = true;
+  n += count;
+  e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_status(e, "add");
+  int h_flag = 0;
+  e = cudaMemcpy(&h_flag, flag, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_status(e, "add flag readback");
+  lo_nonzero = h_flag != 0;
+  return PX_OK;
+}
+
+static px_status flat_check(const px_flat* h) {
+  if (h == nullptr) return set_error(PX_EINVAL, "null handle");
+  return PX_OK;
+}
+
+extern "C" {
+
+PX_API const char* px_last_error(void) { return g_last_error.c_str(); }
+PX_API const char* px_version(void) { return "proxima_b200 0.1.0 (sm_100a)"; }
+
+PX_API int32_t px_device_count(void) {
+  int c = 0;
+  if (cudaGetDeviceCount(&c) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return c;
+}
+
+PX_API px_status px_flat_create(int32_t dim, int32_t metric, const int32_t* devices, int32_t ndev,
+                                px_flat** out) {
+  if (out == nullptr) return set_error(PX_EINVAL, "out is null");
+  *out = nullptr;
+  if (dim <= 0) return set_error(PX_EINVAL, "dim must be > 0");
+  if (metric != PX_METRIC_L2 && metric != PX_METRIC_IP)
+    return set_error(PX_EINVAL, "metric must be 0 (L2) or 1 (inner product)");
+  std::vector<int> devs;
+  px_status s = resolve_devices(devices, ndev, devs);
+  if (s != PX_OK) return s;
+  px_flat* h = new px_flat();
+  h->dim = dim;
+  h->ld = (dim + 31) & ~31;
+  h->metric = metric;
+  h->shards.resize(devs.size());
+  for (size_t i = 0; i < devs.size(); ++i) {
+    FlatShard& sh = h->shards[i];
+    sh.device = devs[i];
+    DeviceGuard g(sh.device);
+    cudaError_t e = cudaStreamCreateWithFlags(&sh.stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc(&sh.flag, 4 * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(sh.flag, 0, 4 * sizeof(int));
+    if (e != cudaSuccess) {
+      px_status st = cuda_status(e, "create");
+      for (auto& x : h->shards) x.release();
+      delete h;
+      return st;
+    }
+    sh.sms = device_sm_count(sh.device);
+  }
+  *out = h;
+  return PX_OK;
+}
+
+PX_API px_status px_flat_destroy(px_flat* h) {
+  if (h == nullptr) return PX_OK;
+  {
+    std::lock_guard<std::mutex> lk(h->mu);
+    for (auto& sh : h->shards) sh.release();
+    h->gather.release_all();
+  }
+  delete h;
+  return PX_OK;
+}
+
+PX_API int64_t px_flat_size(const px_flat* h) { return h ? h->total : 0; }
+PX_API int32_t px_flat_dim(const px_flat* h) { return h ? h->dim : 0; }
+PX_API int32_t px_flat_metric(const px_flat* h) { return h ? h->metric : -1; }
+
+PX_API px_status px_flat_set_id_offset(px_flat* h, int64_t offset) {
+  px_status s = flat_check(h);
+  if (s != PX_OK) return s;
+  if (offset < 0) return set_error(PX_EINVAL, "id offset must be >= 0");
+  h->id_offset = offset;
+  return PX_OK;
+}
+
+PX_API px_status px_flat_add(px_flat* h, const float* rows, int64_t n) {
+  px_status s = flat_check(h);
+  if (s != PX_OK) return s;
+  if (n < 0) return set_error(PX_EINVAL, "row count must be >= 0");
+  if (n == 0) return PX_OK;
+  if (rows == nullptr) return set_error(PX_EINVAL, "rows is null");
+  if (!all_finite(rows, n * h->dim))
+    return set_error(PX_EINVAL, "vectors must not contain NaN or infinite values");
+  std::lock_guard<std::mutex> lk(h->mu);
+  const int G = static_cast<int>(h->shards.size());
+  std::vector<int64_t> begin, count;
+  split_rows(n, G, begin, count);
+  for (int g = 0; g < G; ++g) {
+    if (count[g] == 0) continue;
+    FlatShard& sh = h->shards[g];
+    if (sh.n + count[g] > 0xFFFFFFFFll)
+      return set_error(PX_EUNSUPPORTED, "a shard holds at most 2^32-1 rows");
+    DeviceGuard dg(sh.device);
+    // Stage the run in device memory (contiguous n x dim), then lay it out.
+    const size_t bytes = sizeof(float) * static_cast<size_t>(count[g]) * h->dim;
+    cudaError_t e = sh.stage.reserve(bytes);
+    if (e != cudaSuccess) return cuda_status(e, "staging allocation");
+    e = cudaMemcpyAsync(sh.stage.ptr, rows + begin[g] * h->dim, bytes, cudaMemcpyHostToDevice,
+                        sh.stream);
+    if (e != cudaSuccess) return cuda_status(e, "row upload");
+    s = sh.append_device(static_cast<const float*>(sh.stage.ptr), count[g], h->dim, h->ld,
+                         h->total + begin[g]);
+    if (s != PX_OK) return s;
+  }
+  h->total += n;
+  return PX_OK;
+}
+
+PX_API px_status px_flat_add_device(px_flat* h, const float* d_rows, int64_t n) {
+  px_status s = flat_check(h);
+  if (s != PX_OK) return s;
+  if (h->shards.size() != 1) return set_error(PX_EUNSUPPORTED, "px_flat_add_device needs a single-device handle");
+  if (n < 0) return set_error(PX_EINVAL, "row count must be >= 0");
+  if (n == 0) return PX_OK;
+  std::lock_guard<std::mutex> lk(h->mu);
+  FlatShard& sh = h->shards[0];
+  if (sh.n + n > 0xFFFFFFFFll) return set_error(PX_EUNSUPPORTED, "a shard holds at most 2^32-1 rows");
+  DeviceGuard dg(sh.device);
+  s = sh.append_device(d_rows, n, h->dim, h->ld, h->total);
+  if (s != PX_OK) return s;
+  h->total += n;
+  return PX_OK;
+}
+
+}  // extern "C"
+
+// Runs one shard's search on its device. d_q: nq x dim on the shard's device.
+// Writes nq x k ids (global) and distances (natural or key space).
+static px_status shard_search(const px_flat* h, FlatShard& sh, int metric, const float* d_q,
+                              int64_t nq, int k, const uint8_t* d_mask, bool natural,
+                              int64_t* d_ids, float* d_dists, cudaStream_t stream) {
+  const bool l2 = metric == PX_METRIC_L2;
+  px_status s = sh.segs.sync_device();
+  if (s != PX_OK) return s;
+  SearchPlan plan;
+  s = plan_flat_search(h, sh, nq, k, plan);
+  if (s != PX_OK) return s;
+  cudaError_t e = sh.ws.reserve(plan.ws_bytes);
+  if (e != cudaSuccess) return cuda_status(e, "search workspace allocation");
+  s = run_flat_search(h, sh, plan, metric, d_q, nq, k, d_mask, stream);
+  if (s != PX_OK) return s;
+  e = launch_emit(plan.final_cands, nq, k, l2, natural, sh.segs.view(h->id_offset), d_ids, d_dists,
+                  stream);
+  if (e != cudaSuccess) return cuda_status(e, "emit launch");
+  return PX_OK;
+}
+
+// Full host-to-host search over every shard.
+static px_status flat_search_host(const px_flat* hc, int metric, const float* queries, int64_t nq,
+                                  int32_t k, const uint8_t* mask, bool natural, int64_t* out_ids,
+                                  float* out_dists) {
+  px_flat* h = const_cast<px_flat*>(hc);
+  std::lock_guard<std::mutex> lk(h->mu);
+  const int G = static_cast<int>(h->shards.size());
+  const size_t qbytes = sizeof(float) * static_cast<size_t>(nq) * h->dim;
+  const size_t obytes = static_cast<size_t>(nq) * k;
+  std::vector<uint8_t> local_mask;
+
+  // Per-shard: upload queries (+ mask), search, leave results on device.
+  for (int g = 0; g < G; ++g) {
+    FlatShard& sh = h->shards[g];
+    DeviceGuard dg(sh.device);
+    Carver c;
+    c.take(qbytes);
+    c.take(obytes * sizeof(int64_t));
+    c.take(obytes * sizeof(float));
+    if (mask) c.take(static_cast<size_t>(std::max<int64_t>(sh.n, 1)));
+    cudaError_t e = sh.stage.reserve(c.used);
+    if (e != cudaSuccess) return cuda_status(e, "query staging allocation");
+    c = Carver{sh.stage.ptr};
+    float* d_q = static_cast<float*>(c.take(qbytes));
+    int64_t* d_ids = static_cast<int64_t*>(c.take(obytes * sizeof(int64_t)));
+    float* d_d = static_cast<float*>(c.take(obytes * sizeof(float)));
+    uint8_t* d_mask = nullptr;
+    if (mask) {
+      d_mask = static_cast<uint8_t*>(c.take(static_cast<size_t>(std::max<int64_t>(sh.n, 1))));
+      sh.segs.local_mask(mask, sh.n, local_mask);
+      if (sh.n > 0) {
+        e = cudaMemcpyAsync(d_mask, local_mask.data(), static_cast<size_t>(sh.n), cudaMemcpyHostToDevice,
+                            sh.stream);
+        if (e != cudaSuccess) return cuda_status(e, "mask upload");
+      }
+    }
+    e = cudaMemcpyAsync(d_q, queries, qbytes, cudaMemcpyHostToDevice, sh.stream);
+    if (e != cudaSuccess) return cuda_status(e, "query upload");
+    px_status s = shard_search(h, sh, metric, d_q, nq, k, d_mask, natural && G == 1, d_ids, d_d,
+                               sh.stream);
+    if (s != PX_OK) return s;
+    sh.out_ids = d_ids;
+    sh.out_dists = d_d;
+  }
+
+  FlatShard& s0 = h->shards[0];
+  DeviceGuard dg(s0.device);
+  const int64_t* res_ids = s0.out_ids;
+  const float* res_d = s0.out_dists;
+  if (G > 1) {
+    // Gather every shard's key-space lists on device 0 and merge them.
+    px_status s = h->gather.ensure(s0.device, static_cast<size_t>(G) * obytes);
+    if (s != PX_OK) return s;
+    for (int g = 0; g < G; ++g) {
+      FlatShard& sh = h->shards[g];
+      cudaError_t e = cudaMemcpyPeerAsync(h->gather.ids + g * obytes, s0.device, sh.out_ids,
+                                          sh.device, obytes * sizeof(int64_t), sh.stream);
+      if (e == cudaSuccess)
+        e = cudaMemcpyPeerAsync(h->gather.keys + g * obytes, s0.device, sh.out_dists, sh.device,
+                                obytes * sizeof(float), sh.stream);
+      if (e != cudaSuccess) return cuda_status(e, "shard gather");
+      if (g > 0) {
+        DeviceGuard dgs(sh.device);
+        e = cudaEventRecord(h->gather.events[g], sh.stream);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(s0.stream, h->gather.events[g], 0);
+        if (e != cudaSuccess) return cuda_status(e, "shard gather sync");
+      }
+    }
+    cudaError_t e = launch_merge_shards(h->gather.keys, h->gather.ids, G, nq, k,
+                                        metric == PX_METRIC_L2, natural, h->gather.out_dists,
+                                        h->gather.out_ids, s0.stream);
+    if (e != cudaSuccess) return cuda_status(e, "shard merge launch");
+    res_ids = h->gather.out_ids;
+    res_d = h->gather.out_dists;
+  }
+  cudaError_t e = cudaMemcpyAsync(out_ids, res_ids, obytes * sizeof(int64_t), cudaMemcpyDeviceToHost,
+                                  s0.stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(out_dists, res_d, obytes * sizeof(float), cudaMemcpyDeviceToHost, s0.stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s0.stream);
+  if (e != cudaSuccess) return cuda_status(e, "search");
+  for (int g = 0; g < G; ++g) {
+    px_status s = check_device_flags(h->shards[g]);
+    if (s != PX_OK) return s;
+  }
+  return PX_OK;
+}
+
+static px_status validate_search(const px_flat* h, const float* queries, int64_t nq, int32_t k,
+                                 const int64_t* out_ids, const float* out_dists) {
+  px_status s = flat_check(h);
+  if (s != PX_OK) return s;
+  if (k < 0) return set_error(PX_EINVAL, "k must be >= 0");
+  if (nq < 0) return set_error(PX_EINVAL, "query count must be >= 0");
+  if (k > PX_MAX_K)
+    return set_error(PX_EUNSUPPORTED, "k=" + std::to_string(k) + " exceeds PX_MAX_K=" +
+                                          std::to_string(PX_MAX_K));
+  if (nq > 0 && k > 0 && (queries == nullptr || out_ids == nullptr || out_dists == nullptr))
+    return set_error(PX_EINVAL, "null buffer");
+  return PX_OK;
+}
+
+extern "C" {
+
+PX_API px_status px_flat_search(const px_flat* h, const float* queries, int64_t nq, int32_t k,
+                                int64_t* out_ids, float* out_dists) {
+  px_status s = validate_search(h, queries, nq, k, out_ids, out_dists);
+  if (s != PX_OK) return s;
+  if (k == 0 || nq == 0) return PX_OK;
+  if (!all_finite(queries, nq * h->dim))
+    return set_error(PX_EINVAL, "query must not contain NaN or infinite values");
+  return flat_search_host(h, h->metric, queries, nq, k, nullptr, true, out_ids, out_dists);
+}
+
+PX_API px_status px_flat_search_filtered(const px_flat* h, const float* queries, int64_t nq,
+                                         int32_t k, const uint8_t* mask, int64_t* out_ids,
+                                         float* out_dists) {
+  px_status s = validate_search(h, queries, nq, k, out_ids, out_dists);
+  if (s != PX_OK) return s;
+  if (mask == nullptr && h->total > 0) return set_error(PX_EINVAL, "mask is null");
+  if (k == 0 || nq == 0) return PX_OK;
+  if (!all_finite(queries, nq * h->dim))
+    return set_error(PX_EINVAL, "query must not contain NaN or infinite values");
+  return flat_search_host(h, h->metric, queries, nq, k, mask, true, out_ids, out_dists);
+}
+
+PX_API px_status px_flat_search_device(const px_flat* hc, const float* d_queries, int64_t nq,
+                                       int32_t k, int32_t key_space, int64_t* d_out_ids,
+                                       float* d_out_dists, void* stream) {
+  px_status s = validate_search(hc, d_queries, nq, k, d_out_ids, d_out_dists);
+  if (s != PX_OK) return s;
+  if (hc->shards.size() != 1)
+    return set_error(PX_EUNSUPPORTED, "px_flat_search_device needs a single-device handle");
+  if (k == 0 || nq == 0) return PX_OK;
+  px_flat* h = const_cast<px_flat*>(hc);
+  std::lock_guard<std::mutex> lk(h->mu);
+  FlatShard& sh = h->shards[0];
+  DeviceGuard dg(sh.device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : sh.stream;
+  return shard_search(h, sh, h->metric, d_queries, nq, k, nullptr, key_space == 0, d_out_ids,
+                      d_out_dists, st);
+}
+
+PX_API px_status px_merge_shards_device(int32_t device, const float* d_keys, const int64_t* d_ids,
+                                        int32_t nshard, int64_t nq, int32_t k, int32_t metric,
+                                        int32_t natural, float* d_out_dists, int64_t* d_out_ids,
+                                        void* stream) {
+  if (nshard < 1 || nshard > 8) return set_error(PX_EINVAL, "nshard must be in 1..=8");
+  if (k < 0 || nq < 0) return set_error(PX_EINVAL, "negative size");
+  if (metric != PX_METRIC_L2 && metric != PX_METRIC_IP) return set_error(PX_EINVAL, "bad metric");
+  DeviceGuard dg(device);
+  cudaError_t e = launch_merge_shards(d_keys, d_ids, nshard, nq, k, metric == PX_METRIC_L2,
+                                      natural != 0, d_out_dists, d_out_ids,
+                                      static_cast<cudaStream_t>(stream));
+  return cuda_status(e, "merge_shards launch");
+}
+
+// ---- reference-compatible ABI (knn.cu:123-180) ----------------------------
+
+struct PxGpuIndex {
+  px_flat* flat;
+};
+
+PX_API PxGpuIndex* knn_gpu_create(const float* base, int n, int dim) {
+  if (n < 0 || dim <= 0 || (n > 0 && base == nullptr)) return nullptr;
+  px_flat* f = nullptr;
+  if (px_flat_create(dim, PX_METRIC_L2, nullptr, 0, &f) != PX_OK) return nullptr;
+  if (n > 0) {
+    // The reference copies the base without checking values (knn.cu:130-141).
+    std::lock_guard<std::mutex> lk(f->mu);
+    FlatShard& sh = f->shards[0];
+    DeviceGuard dg(sh.device);
+    const size_t bytes = sizeof(float) * static_cast<size_t>(n) * dim;
+    if (sh.stage.reserve(bytes) != cudaSuccess ||
+        cudaMemcpyAsync(sh.stage.ptr, base, bytes, cudaMemcpyHostToDevice, sh.stream) != cudaSuccess ||
+        sh.append_device(static_cast<const float*>(sh.stage.ptr), n, dim, f->ld, 0) != PX_OK) {
+      px_flat_destroy(f);
+      return nullptr;
+    }
+    f->total = n;
+  }
+  return new PxGpuIndex{f};
+}
+
+PX_API int knn_gpu_search(const PxGpuIndex* idx, const float* queries, int nq, int k, int metric,
+                          long long* out_ids, float* out_keys) {
+  if (k < 1 || k > PX_MAX_K) return -1;
+  if (idx == nullptr || nq < 0) return static_cast<int>(cudaErrorInvalidValue);
+  if (nq == 0) return 0;
+  if (metric != PX_METRIC_L2 && metric != PX_METRIC_IP) return static_cast<int>(cudaErrorInvalidValue);
+  px_status s = flat_search_host(idx->flat, metric, queries, nq, k, nullptr, false,
+                                 reinterpret_cast<int64_t*>(out_ids), out_keys);
+  if (s == PX_OK) return 0;
+  cudaError_t last = cudaGetLastError();
+  return static_cast<int>(last != cudaSuccess ? last : cudaErrorUnknown);
+}
+
+PX_API void knn_gpu_free(PxGpuIndex* idx) {
+  if (!idx) return;
+  px_flat_destroy(idx->flat);
+  delete idx;
+}
+
+}  // extern "C"

@@ -1,0 +1,99 @@
+// Launch interfaces of the proxima_b200 kernels (internal to the library).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace px {
+
+// ---- K2: exact streaming scan (k_exact.cu) --------------------------------
+struct ExactScanArgs {
+  const float* base;       // shard rows, row stride ld floats
+  int64_t n;               // rows in the shard
+  int ld;                  // row stride (floats), multiple of 4
+  int d;                   // dimension
+  const float* queries;    // nq x d, contiguous
+  int nq;
+  int k;
+  int group;               // queries per CTA: 1, 2, 4 or 8
+  int ncta;                // row splits (gridDim.x)
+  int64_t rows_per_cta;
+  const uint8_t* mask;     // optional per-row filter (nonzero = keep)
+  bool l2;
+  uint64_t* partial;       // [nq][ncta][k] sorted candidate lists
+};
+cudaError_t launch_exact_scan(const ExactScanArgs& a, cudaStream_t stream);
+int exact_max_k();
+int exact_group_for(int64_t nq);
+int exact_buf_for(int k);
+size_t exact_smem_for(int group, int k, int d);
+
+// ---- merges and output (k_merge.cu) ---------------------------------------
+// Selects, per query, the k smallest of `nlists` sorted lists of packed
+// candidates ([nq][nlists][list_len], PX_EMPTY-padded) into out [nq][k].
+cudaError_t launch_merge_lists(const uint64_t* lists, int64_t nq, int nlists, int list_len, int k,
+                               uint64_t* out, cudaStream_t stream);
+
+// Converts packed candidates [nq][k] into caller ids / distances.
+// natural: sqrt / negate as FlatIndex::scan reports (flat.rs:139-147);
+// otherwise key space (squared L2, negated IP) as knn_gpu_search reports.
+// Row -> global id through `nseg` segments (local_begin, global_begin) sorted
+// by local_begin, plus id_offset.
+struct IdSegments {
+  const int64_t* local_begin;  // device, nseg
+  const int64_t* global_begin; // device, nseg
+  int nseg;
+  int64_t id_offset;
+};
+cudaError_t launch_emit(const uint64_t* cands, int64_t nq, int k, bool l2, bool natural,
+                        IdSegments segs, int64_t* out_ids, float* out_dists,
+                        cudaStream_t stream);
+
+// Cross-shard merge (K6): G sorted lists per query of (key, global id) pairs,
+// layout [G][nq][k] in key space. Ties on key break by the smaller global id.
+// Writes natural or key-space distances.
+cudaError_t launch_merge_shards(const float* keys, const int64_t* ids, int nshard, int64_t nq,
+                                int k, bool l2, bool natural, float* out_dists, int64_t* out_ids,
+                                cudaStream_t stream);
+
+// ---- PQ (k_pq.cu) ---------------------------------------------------------
+// ADC tables (pq.rs:123-136): lut [nq][m][ksub].
+cudaError_t launch_pq_lut(const float* books, int m, int ksub, int dsub, bool l2,
+                          const float* queries, int nq, float* lut, cudaStream_t stream);
+
+struct PqScanArgs {
+  const uint8_t* codes;    // n x m
+  int64_t n;
+  int m;
+  int ksub;
+  const float* lut;        // [nq][m][ksub]
+  int nq;
+  int k;
+  int group;               // queries per CTA
+  int ncta;
+  int64_t rows_per_cta;
+  const uint8_t* mask;
+  uint64_t* partial;       // [nq][ncta][k]
+};
+cudaError_t launch_pq_scan(const PqScanArgs& a, cudaStream_t stream);
+int pq_group_for(int m, int ksub, int64_t nq);
+size_t pq_smem_for(int group, int m, int ksub, int k);
+int pq_max_k();
+
+// Nearest centroid per (vector, subspace) with the reference's strict '<'
+// first-wins rule (pq.rs:107-121, 155-167). vectors: n x (m*dsub).
+cudaError_t launch_nearest_centroid(const float* vectors, int64_t n, int m, int dsub, int ksub,
+                                    const float* books, uint32_t* out_assign, uint8_t* out_codes,
+                                    cudaStream_t stream);
+
+// ---- shard preparation (k_prep.cu) ----------------------------------------
+// Copies n rows of d floats into the shard (stride ld, zero padded), and
+// writes the tf32 hi/lo split planes and the squared norms.
+cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, float* dst,
+                                float* hi, float* lo, float* norms, int* lo_nonzero,
+                                cudaStream_t stream);
+cudaError_t launch_split_queries(const float* q, int64_t nq, int d, int ld, int64_t rows_alloc,
+                                 float* hi, float* lo, float* norms, int* lo_nonzero,
+                                 cudaStream_t stream);
+
+}  // namespace px

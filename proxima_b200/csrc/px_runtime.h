@@ -1,0 +1,125 @@
+// Host-side runtime structures shared by the C ABI translation units.
+#pragma once
+
+#include <cstdint>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "../../include/px.h"
+#include "px_kernels.h"
+
+namespace px {
+
+extern thread_local std::string g_last_error;
+px_status set_error(px_status s, const std::string& msg);
+px_status cuda_status(cudaError_t e, const char* what);
+bool all_finite(const float* p, int64_t count);
+int device_sm_count(int dev);
+px_status resolve_devices(const int32_t* devices, int32_t ndev, std::vector<int>& out);
+void split_rows(int64_t n, int parts, std::vector<int64_t>& begin, std::vector<int64_t>& count);
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev);
+  ~DeviceGuard();
+};
+
+// Grow-only device allocation (freed explicitly by the owner).
+struct DevBuf {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  cudaError_t reserve(size_t need);
+  void release();
+};
+
+struct Carver {
+  void* base = nullptr;
+  size_t used = 0;
+  Carver() = default;
+  explicit Carver(void* b) : base(b) {}
+  void* take(size_t bytes);
+};
+
+// Maps shard-local rows to global ids: one (local_begin, global_begin) pair
+// per add() run that reached this shard.
+struct Segments {
+  std::vector<int64_t> local, global;
+  DevBuf dev;
+  bool dirty = true;
+  px_status sync_device();
+  IdSegments view(int64_t id_offset) const;
+  void local_mask(const uint8_t* global_mask, int64_t n_local, std::vector<uint8_t>& out) const;
+};
+
+}  // namespace px
+
+struct FlatShard {
+  int device = 0;
+  int sms = 148;
+  cudaStream_t stream = nullptr;
+  float* x = nullptr;      // fp32 rows, stride ld
+  float* hi = nullptr;     // tf32(x)
+  float* lo = nullptr;     // tf32(x - hi)
+  float* norms = nullptr;  // squared norms
+  int64_t n = 0, cap = 0;
+  int* flag = nullptr;     // [0] lo plane nonzero, [1] device error code
+  bool lo_nonzero = false;
+  px::Segments segs;
+  px::DevBuf ws;           // search workspace
+  px::DevBuf stage;        // uploads (queries, rows, masks, outputs)
+  int64_t* out_ids = nullptr;  // results of the last search (inside stage)
+  float* out_dists = nullptr;
+
+  px_status ensure_capacity(int64_t need, int ld);
+  px_status append_device(const float* d_src, int64_t count, int d, int ld, int64_t global_begin);
+  void release();
+};
+
+// Device-0 buffers for gathering the shards' lists in a multi-device handle.
+struct GatherBuf {
+  int device = -1;
+  size_t cap = 0;
+  float* keys = nullptr;
+  int64_t* ids = nullptr;
+  float* out_dists = nullptr;
+  int64_t* out_ids = nullptr;
+  cudaEvent_t events[8] = {};
+  px_status ensure(int dev, size_t entries);
+  void release_all();
+};
+
+struct px_flat {
+  int dim = 0;
+  int ld = 0;
+  int metric = 0;
+  int64_t total = 0;
+  int64_t id_offset = 0;
+  std::vector<FlatShard> shards;
+  GatherBuf gather;
+  std::mutex mu;
+};
+
+namespace px {
+
+enum class FlatPath { Exact = 0, Gemm = 1 };
+
+struct SearchPlan {
+  FlatPath path = FlatPath::Exact;
+  int group = 1;
+  int ncta = 1;
+  int64_t rows_per_cta = 0;
+  size_t ws_bytes = 0;
+  uint64_t* partial = nullptr;
+  uint64_t* final_cands = nullptr;
+};
+
+px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, int k, SearchPlan& plan);
+px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int metric,
+                          const float* d_q, int64_t nq, int k, const uint8_t* d_mask,
+                          cudaStream_t stream);
+px_status check_device_flags(FlatShard& sh);
+
+}  // namespace px

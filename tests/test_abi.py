@@ -1,0 +1,104 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol
+include/*.h declares, and fails cleanly (status + message, no abort) when no
+CUDA device is present."""
+
+import ctypes
+import glob
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = []
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = open(h).read()
+        names += re.findall(r"PX_API\s+[\w\s\*]+?\b(\w+)\s*\(", text)
+    return sorted(set(names))
+
+
+def test_header_declares_the_reference_abi():
+    names = declared_symbols()
+    # crates/core/src/gpu.rs:10-15 binds exactly these three.
+    for n in ("knn_gpu_create", "knn_gpu_search", "knn_gpu_free"):
+        assert n in names
+    assert len(names) >= 25
+
+
+def test_library_exports_every_declared_symbol(px):
+    lib = px._lib.load()
+    missing = [n for n in declared_symbols() if not hasattr(lib, n)]
+    assert not missing, missing
+    # And the Python binding types every one of them.
+    assert set(declared_symbols()) <= set(px._lib.SIGNATURES)
+
+
+def test_exports_are_c_symbols():
+    so = os.path.join(ROOT, "proxima_b200", "libproxima_b200.so")
+    out = subprocess.run(["nm", "-D", "--defined-only", so], capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    for n in declared_symbols():
+        assert n in exported, n  # unmangled, default visibility
+
+
+def test_build_targets_sm100a_only():
+    from proxima_b200 import build
+    assert build.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def test_no_gpu_errors_are_reported(px):
+    lib = px._lib.load()
+    if lib.px_device_count() > 0:
+        pytest.skip("a GPU is present")
+    h = ctypes.c_void_p()
+    st = lib.px_flat_create(16, 0, None, 0, ctypes.byref(h))
+    assert st == px._lib.PX_ECUDA
+    assert "no CUDA device" in px._lib.last_error()
+    assert lib.knn_gpu_create(None, 0, 4) is None
+    with pytest.raises(px.PxError):
+        px.FlatIndex(16)
+
+
+def test_argument_validation_without_gpu(px):
+    lib = px._lib.load()
+    h = ctypes.c_void_p()
+    assert lib.px_flat_create(0, 0, None, 0, ctypes.byref(h)) == px._lib.PX_EINVAL
+    assert "dim must be > 0" in px._lib.last_error()
+    assert lib.px_flat_create(4, 7, None, 0, ctypes.byref(h)) == px._lib.PX_EINVAL
+    assert lib.px_pq_create(10, 3, 8, 0, None, None, 0, ctypes.byref(h)) == px._lib.PX_EINVAL
+    assert "divisible by m" in px._lib.last_error()
+    assert lib.px_pq_create(8, 2, 9, 0, None, None, 0, ctypes.byref(h)) == px._lib.PX_EINVAL
+    assert "nbits" in px._lib.last_error()
+    # knn_gpu_search rejects k < 1 before touching the index (knn.cu:145).
+    assert lib.knn_gpu_search(None, None, 1, 0, 0, None, None) == -1
+    assert lib.knn_gpu_search(None, None, 1, px.PX_MAX_K + 1, 0, None, None) == -1
+    # Null handles are tolerated by destroy/free.
+    assert lib.px_flat_destroy(None) == 0
+    lib.knn_gpu_free(None)
+
+
+def test_python_mirror_validation_without_gpu(px):
+    # Checks that run before any device call, as in the PyO3 layer.
+    with pytest.raises(ValueError, match="dim must be > 0"):
+        px.FlatIndex(0)
+    with pytest.raises(OverflowError):
+        px.FlatIndex(-1)
+    with pytest.raises(ValueError):
+        px.PqIndex(dim=10, m=3)
+    with pytest.raises(ValueError):
+        px.PqIndex(dim=8, m=0)
+    with pytest.raises(ValueError):
+        px.PqIndex(dim=8, m=2, nbits=9)
+    pq = px.PqIndex(dim=64, metric=px.Metric.L2, m=8)
+    assert not pq.is_trained and pq.size == 0 and pq.memory_bytes == 0
+    with pytest.raises(ValueError, match="not trained"):
+        pq.add(np.zeros((4, 64), np.float32))
+    with pytest.raises(ValueError, match="not trained"):
+        pq.search(np.zeros(64, np.float32), k=5)
+    with pytest.raises(ValueError, match="not trained"):
+        pq.search_filtered(np.zeros(64, np.float32), np.zeros(0, bool), k=5)

@@ -1,0 +1,260 @@
+"""GPU parity of FlatIndex (exact kNN) against the CPU oracle.
+
+Every case compares the sm_100a path, called through the C ABI, with the
+oracle's restatement of FlatIndex::search_batch (crates/core/src/flat.rs)
+using the tie-aware, bit-exact rule of tests/_parity.py.
+"""
+
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from tests import _data, _parity
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "flat_pq_golden.npz")
+
+
+@pytest.fixture(scope="module")
+def pxm(px, oracle_lib):
+    assert px.device_count() > 0, "GPU tests need a CUDA device"
+    return px
+
+
+def _metric(pxm, m):
+    return pxm.Metric.L2 if m == O.L2 else pxm.Metric.InnerProduct
+
+
+def _run(pxm, data, metric, queries, k, adds=1, filter_=None):
+    idx = pxm.FlatIndex(data.shape[1], _metric(pxm, metric))
+    for part in np.array_split(data, adds):
+        idx.add(np.ascontiguousarray(part))
+    if filter_ is None:
+        return idx.search_batch(queries, k=k)
+    return idx.search_batch_filtered(queries, filter_, k=k)
+
+
+@pytest.mark.parametrize("metric", [O.L2, O.IP])
+@pytest.mark.parametrize("n,dim,nq,k", [
+    (1000, 24, 1, 10), (1000, 24, 7, 10), (5000, 64, 33, 5), (2000, 12, 9, 1),
+    (3000, 7, 5, 17), (777, 3, 4, 100), (4000, 128, 64, 10), (300, 16, 2, 300),
+])
+def test_uniform_parity(pxm, metric, n, dim, nq, k):
+    data = O.gen_uniform(n, dim, 7 + n)
+    queries = O.gen_uniform(nq, dim, 999 + dim)
+    ids, d = _run(pxm, data, metric, queries, k)
+    _parity.check_flat(data, metric, queries, ids, d, k)
+
+
+def test_golden_fixture(pxm):
+    g = np.load(GOLDEN)
+    data = O.gen_uniform(int(g["n"]), int(g["dim"]), int(g["seed_base"]))
+    queries = O.gen_uniform(int(g["nq"]), int(g["dim"]), int(g["seed_query"]))
+    k = int(g["k"])
+    for metric, name in ((O.L2, "l2"), (O.IP, "ip")):
+        ids, d = _run(pxm, data, metric, queries, k)
+        _parity.check(ids, d, g[f"flat_{name}_ids"], g[f"flat_{name}_dists"],
+                      _parity.flat_natural(data, metric, queries))
+
+
+def test_config1_shape_ip(pxm):
+    # Config 1's distribution (unit-norm N(0,1), d=384, IP), fewer rows.
+    data = _data.unit_gaussian(20000, 384, 1)
+    queries = _data.unit_gaussian(16, 384, 2)
+    ids, d = _run(pxm, data, O.IP, queries, 10)
+    _parity.check_flat(data, O.IP, queries, ids, d, 10)
+
+
+def test_config2_shape_l2_with_ties(pxm):
+    # Config 2's distribution (integer-valued SIFT-like mixture, L2).
+    data, queries = _data.sift_like(50000, 24, seed=3, centres=100)
+    ids, d = _run(pxm, data, O.L2, queries, 10)
+    _parity.check_flat(data, O.L2, queries, ids, d, 10)
+    # Duplicated rows force exact ties at every rank.
+    dup = np.repeat(data[:500], 3, axis=0)
+    ids, d = _run(pxm, dup, O.L2, dup[:8] + 1.0, 10)
+    _parity.check_flat(dup, O.L2, dup[:8] + 1.0, ids, d, 10)
+
+
+def test_config5_shape_l2(pxm):
+    data, queries = _data.gaussian_mixture(30000, 12, centres=300, seed=5)
+    ids, d = _run(pxm, data, O.L2, queries, 10)
+    _parity.check_flat(data, O.L2, queries, ids, d, 10)
+
+
+def test_incremental_adds_keep_global_ids(pxm):
+    data = O.gen_uniform(4000, 32, 21)
+    queries = O.gen_uniform(9, 32, 22)
+    ids, d = _run(pxm, data, O.L2, queries, 10, adds=5)
+    _parity.check_flat(data, O.L2, queries, ids, d, 10)
+
+
+@pytest.mark.parametrize("metric", [O.L2, O.IP])
+def test_filtered_parity(pxm, metric):
+    data = O.gen_uniform(3000, 48, 31)
+    queries = O.gen_uniform(6, 48, 32)
+    rng = np.random.default_rng(1)
+    for mask in (rng.random(3000) < 0.2, np.zeros(3000, bool), np.arange(3000) == 17):
+        ids, d = _run(pxm, data, metric, queries, 10, filter_=mask)
+        _parity.check_flat(data, metric, queries, ids, d, 10, filter_=mask)
+
+
+def test_empty_and_small_index(pxm):
+    idx = pxm.FlatIndex(4, pxm.Metric.L2)
+    ids, d = idx.search(np.zeros(4, np.float32), k=3)
+    assert ids.tolist() == [-1, -1, -1]
+    assert d.tolist() == [np.finfo(np.float32).max] * 3
+    idx.add(np.array([[0, 0, 0, 0], [1, 1, 1, 1]], np.float32))
+    ids, d = idx.search(np.zeros(4, np.float32), k=5)
+    assert ids.tolist() == [0, 1, -1, -1, -1]
+    assert d.tolist()[:2] == [0.0, 2.0]
+    ids, d = idx.search(np.zeros(4, np.float32), k=0)
+    assert ids.shape == (0,) and d.shape == (0,)
+    ipx = pxm.FlatIndex(4, pxm.Metric.InnerProduct)
+    ipx.add(np.ones((1, 4), np.float32))
+    ids, d = ipx.search(np.ones(4, np.float32), k=3)
+    assert ids.tolist() == [0, -1, -1]
+    assert d.tolist()[1:] == [-np.finfo(np.float32).max] * 2
+
+
+def test_errors_are_reported(pxm):
+    idx = pxm.FlatIndex(8, pxm.Metric.L2)
+    with pytest.raises(ValueError):
+        idx.add(np.zeros((10, 9), np.float32))
+    with pytest.raises(ValueError, match="NaN"):
+        idx.add(np.full((1, 8), np.nan, np.float32))
+    idx.add(np.zeros((10, 8), np.float32))
+    with pytest.raises(ValueError):
+        idx.search(np.zeros(7, np.float32), k=3)
+    with pytest.raises(ValueError, match="NaN"):
+        idx.search(np.full(8, np.inf, np.float32), k=3)
+    with pytest.raises(ValueError):
+        idx.search(np.zeros(8, np.float32), k=pxm.PX_MAX_K + 1)
+    with pytest.raises(ValueError, match="mask length"):
+        idx.search_filtered(np.zeros(8, np.float32), np.zeros(9, bool), k=3)
+    with pytest.raises(TypeError):
+        idx.add(np.zeros((10, 8), np.float64))
+
+
+# ---- the reference's tests/test_engine.py, run against this package ------
+
+def _normalize(x):
+    return x / np.linalg.norm(x, axis=-1, keepdims=True)
+
+
+@pytest.fixture(scope="module")
+def engine_data():
+    rng = np.random.default_rng(0)
+    return _normalize(rng.standard_normal((3000, 64)).astype(np.float32))
+
+
+def test_engine_inner_product_matches_numpy(pxm, engine_data):
+    idx = pxm.FlatIndex(dim=64, metric=pxm.Metric.InnerProduct)
+    idx.add(engine_data)
+    q = _normalize(np.random.default_rng(1).standard_normal(64).astype(np.float32))
+    ids, sims = idx.search(q, k=10)
+    ref = np.argsort(-(engine_data @ q))[:10]
+    assert set(ids.tolist()) == set(ref.tolist())
+    for i, s in zip(ids.tolist(), sims.tolist()):
+        assert abs(s - float(engine_data[i] @ q)) < 1e-4
+
+
+def test_engine_l2_matches_numpy(pxm, engine_data):
+    idx = pxm.FlatIndex(dim=64, metric=pxm.Metric.L2)
+    idx.add(engine_data)
+    q = _normalize(np.random.default_rng(2).standard_normal(64).astype(np.float32))
+    ids, dists = idx.search(q, k=10)
+    d_all = np.linalg.norm(engine_data - q, axis=1)
+    ref = np.argsort(d_all)[:10]
+    assert set(ids.tolist()) == set(ref.tolist())
+    assert np.all(np.diff(dists) >= -1e-4)
+    assert abs(dists[0] - d_all[ref[0]]) < 1e-3
+
+
+def test_engine_self_is_nearest(pxm, engine_data):
+    idx = pxm.FlatIndex(dim=64, metric=pxm.Metric.InnerProduct)
+    idx.add(engine_data)
+    for i in (0, 100, 2999):
+        ids, sims = idx.search(engine_data[i].copy(), k=1)
+        assert ids[0] == i
+        assert sims[0] == pytest.approx(1.0, abs=1e-3)
+
+
+def test_engine_batch_equals_single(pxm, engine_data):
+    idx = pxm.FlatIndex(dim=64, metric=pxm.Metric.InnerProduct)
+    idx.add(engine_data)
+    queries = _normalize(np.random.default_rng(3).standard_normal((50, 64)).astype(np.float32))
+    bids, _ = idx.search_batch(queries, k=8, num_threads=4)
+    for qi in range(len(queries)):
+        sids, _ = idx.search(queries[qi], k=8)
+        assert bids[qi].tolist() == sids.tolist()
+
+
+def test_engine_padding_and_metadata(pxm):
+    idx = pxm.FlatIndex(dim=4, metric=pxm.Metric.L2)
+    idx.add(np.eye(3, 4, dtype=np.float32))
+    ids, _ = idx.search(np.zeros(4, dtype=np.float32), k=5)
+    assert (ids[3:] == -1).all()
+    assert sorted(ids[:3].tolist()) == [0, 1, 2]
+    m = pxm.FlatIndex(dim=16, metric=pxm.Metric.L2)
+    assert m.metric == pxm.Metric.L2 and m.dim == 16
+    m.add(np.zeros((4, 16), dtype=np.float32))
+    assert m.memory_bytes == 4 * 16 * 4 and len(m) == m.size == 4
+
+
+def test_engine_non_contiguous_input_not_corrupted(pxm, engine_data):
+    for metric in (pxm.Metric.InnerProduct, pxm.Metric.L2):
+        idx = pxm.FlatIndex(dim=64, metric=metric)
+        idx.add(np.asfortranarray(engine_data))
+        for i in (0, 123, 2999):
+            ids, _ = idx.search(np.ascontiguousarray(engine_data[i]), k=1)
+            assert ids[0] == i
+    idx = pxm.FlatIndex(dim=64, metric=pxm.Metric.L2)
+    idx.add(engine_data)
+    strided = np.zeros(128, dtype=np.float32)[::2]
+    strided[:] = engine_data[42]
+    ids, _ = idx.search(strided, k=1)
+    assert ids[0] == 42
+
+
+# ---- the reference's C ABI (knn.cu / gpu.rs), called as gpu.rs does -------
+
+@pytest.mark.parametrize("metric", [O.L2, O.IP])
+def test_knn_gpu_abi_key_space(pxm, metric):
+    lib = pxm._lib.load()
+    n, dim, nq, k = 5000, 40, 11, 12
+    data = O.gen_uniform(n, dim, 1)
+    queries = O.gen_uniform(nq, dim, 2)
+    f32p = ctypes.POINTER(ctypes.c_float)
+    h = lib.knn_gpu_create(data.ctypes.data_as(f32p), n, dim)
+    assert h
+    try:
+        ids = np.zeros(nq * k, np.int64)
+        keys = np.zeros(nq * k, np.float32)
+        rc = lib.knn_gpu_search(h, queries.ctypes.data_as(f32p), nq, k, metric,
+                                ids.ctypes.data_as(ctypes.POINTER(ctypes.c_longlong)),
+                                keys.ctypes.data_as(f32p))
+        assert rc == 0
+        assert lib.knn_gpu_search(h, queries.ctypes.data_as(f32p), nq, 0, metric, None, None) == -1
+    finally:
+        lib.knn_gpu_free(h)
+    # gpu.rs:80-93 turns keys into natural distances.
+    nat = np.sqrt(keys) if metric == O.L2 else -keys
+    _parity.check_flat(data, metric, queries, ids.reshape(nq, k), nat.reshape(nq, k), k)
+
+
+def test_multi_device_handle_if_available(pxm):
+    ndev = pxm.device_count()
+    if ndev < 2:
+        pytest.skip("one GPU visible")
+    data = O.gen_uniform(9001, 32, 41)
+    queries = O.gen_uniform(13, 32, 42)
+    idx = pxm.FlatIndex(32, pxm.Metric.L2, devices=list(range(min(ndev, 4))))
+    idx.add(data[:5000])
+    idx.add(data[5000:])
+    ids, d = idx.search_batch(queries, k=10)
+    _parity.check_flat(data, O.L2, queries, ids, d, 10)
