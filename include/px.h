@@ -98,6 +98,28 @@ PX_API int64_t px_flat_size(const px_flat* h);
 PX_API int32_t px_flat_dim(const px_flat* h);
 PX_API int32_t px_flat_metric(const px_flat* h);
 
+/* Kernel path for flat searches: AUTO picks the exact streaming scan for
+ * small batches (and masks) and the tensor-core path otherwise; EXACT and
+ * TENSOR force one (TENSOR fails with PX_EUNSUPPORTED where it cannot serve
+ * the request, e.g. k > 40 or a mask). Results are identical on every path. */
+enum { PX_PATH_AUTO = 0, PX_PATH_EXACT = 1, PX_PATH_TENSOR = 2 };
+PX_API px_status px_flat_set_path(px_flat* h, int32_t mode);
+
+/* Per-search instrumentation (off by default). With profiling on, the
+ * dominant kernel of each search is bracketed by CUDA events on the
+ * launching stream; px_flat_last_profile waits for them and reports. */
+typedef struct px_search_profile {
+  int32_t path;             /* 0 exact scan, 1 tensor-core path */
+  int32_t launches;         /* kernels the search launched on the first shard */
+  int32_t fallback_queries; /* queries re-run by the exact scan (certificate) */
+  int32_t profiled;         /* 1 if main_kernel_ms is valid */
+  float main_kernel_ms;     /* device time of the dominant kernel */
+} px_search_profile;
+PX_API void px_set_profiling(int32_t enable);
+PX_API px_status px_flat_last_profile(const px_flat* h, px_search_profile* out);
+/* Total kernels launched by this library in this process. */
+PX_API int64_t px_launch_count(void);
+
 /* Adds `offset` to every id the handle returns (for a rank that holds rows
  * [offset, offset + size) of a base sharded across processes). */
 PX_API px_status px_flat_set_id_offset(px_flat* h, int64_t offset);

@@ -7,7 +7,8 @@ and persistence of the reference are not part of this package.
 """
 
 from ._core import FlatIndex, Metric, PqIndex, PX_MAX_K, PxError  # noqa: F401
-from ._lib import device_count, LIB_PATH  # noqa: F401
+from ._lib import device_count, launch_count, set_profiling, LIB_PATH  # noqa: F401
 
-__all__ = ["FlatIndex", "PqIndex", "Metric", "PxError", "PX_MAX_K", "device_count"]
+__all__ = ["FlatIndex", "PqIndex", "Metric", "PxError", "PX_MAX_K", "device_count",
+           "launch_count", "set_profiling"]
 __version__ = "0.1.0"

@@ -202,6 +202,24 @@ class FlatIndex:
         """The px_flat* handle (for callers that drive the C ABI directly)."""
         return self._h
 
+    _PATHS = {"auto": 0, "exact": 1, "tensor": 2}
+
+    def set_search_path(self, path: str) -> None:
+        """Kernel path for searches: "auto" (default), "exact" (streaming
+        scan) or "tensor" (tcgen05 3xTF32 + exact rescoring). Results are
+        identical on every path; this only changes speed."""
+        _lib.check(self._lib.px_flat_set_path(self._h, self._PATHS[path]))
+
+    def last_search_profile(self) -> dict:
+        """Path, kernel launches, certificate fallbacks and (when profiling is
+        on, see proxima_b200.set_profiling) the dominant kernel's device time
+        of the last search."""
+        prof = _lib.SearchProfile()
+        _lib.check(self._lib.px_flat_last_profile(self._h, ctypes.byref(prof)))
+        return {"path": ("exact", "tensor")[prof.path], "launches": prof.launches,
+                "fallback_queries": prof.fallback_queries,
+                "main_kernel_ms": prof.main_kernel_ms if prof.profiled else None}
+
 
 class PqIndex:
     """Product-quantized index (crates/core/src/pq.rs:218-396) on the GPU."""

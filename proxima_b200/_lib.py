@@ -41,6 +41,13 @@ _i32p = _c.POINTER(_c.c_int32)
 _u8p = _c.POINTER(_c.c_uint8)
 _llp = _c.POINTER(_c.c_longlong)
 
+class SearchProfile(ctypes.Structure):
+    """px_search_profile (include/px.h)."""
+    _fields_ = [("path", ctypes.c_int32), ("launches", ctypes.c_int32),
+                ("fallback_queries", ctypes.c_int32), ("profiled", ctypes.c_int32),
+                ("main_kernel_ms", ctypes.c_float)]
+
+
 SIGNATURES = {
     "px_last_error": (_c.c_char_p, []),
     "px_version": (_c.c_char_p, []),
@@ -56,6 +63,10 @@ SIGNATURES = {
     "px_flat_dim": (_i32, [_vp]),
     "px_flat_metric": (_i32, [_vp]),
     "px_flat_set_id_offset": (_i32, [_vp, _i64]),
+    "px_flat_set_path": (_i32, [_vp, _i32]),
+    "px_set_profiling": (None, [_i32]),
+    "px_flat_last_profile": (_i32, [_vp, _vp]),
+    "px_launch_count": (_i64, []),
     "px_flat_search": (_i32, [_vp, _f32p, _i64, _i32, _i64p, _f32p]),
     "px_flat_search_filtered": (_i32, [_vp, _f32p, _i64, _i32, _u8p, _i64p, _f32p]),
     "px_flat_search_device": (_i32, [_vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp]),
@@ -111,3 +122,13 @@ def check(status: int) -> None:
 
 def device_count() -> int:
     return int(load().px_device_count())
+
+
+def set_profiling(enable: bool) -> None:
+    """Brackets each search's dominant kernel with CUDA events (see px.h)."""
+    load().px_set_profiling(1 if enable else 0)
+
+
+def launch_count() -> int:
+    """Kernels launched by libproxima_b200 in this process so far."""
+    return int(load().px_launch_count())

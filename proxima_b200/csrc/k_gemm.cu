@@ -1,0 +1,393 @@
+// K1: batched exact-kNN candidate generation on the 5th-generation tensor
+// cores, with the top-k selection fused into the epilogue.
+//
+// The query x base distance matrix is a dense contraction; this kernel
+// computes it tile by tile in TMEM and never writes it to HBM. Operands are
+// the tf32 split planes of the queries and the shard (hi = tf32(x),
+// lo = tf32(x - hi)); each 128 x 256 output tile accumulates
+//     qhi.xhi + qhi.xlo + qlo.xhi            (3xTF32, ~fp32 accurate)
+// and skips a cross term whenever the corresponding lo plane is all zeros
+// (integer-valued data is exact in one pass). The epilogue turns each
+// accumulator into an approximate key (||x||^2 - 2 q.x for L2, -q.x for
+// inner product) and keeps, per query, the CAP smallest keys in registers.
+// Exactness is restored afterwards: the CAP candidates are rescored in the
+// reference's arithmetic and certified against the error bound of this
+// approximation (k_rescore.cu).
+//
+// CTA roles (192 threads, one CTA per SM):
+//   warp 0      TMA producer: 4-stage ring of {Qhi, Qlo, Xhi, Xlo} K-slices
+//   warp 1      TMEM owner and MMA issuer (one elected thread)
+//   warps 2..5  epilogue: TMEM -> registers -> per-query top-CAP lists
+// Two 256-column fp32 accumulators (all 512 TMEM columns) let the epilogue
+// drain tile t while the tensor core fills tile t+1.
+//
+// Work items are (query tile, contiguous run of base tiles); a persistent CTA
+// walks items blockIdx.x, +gridDim.x, ... Items are ordered run-major, so
+// the CTAs of one wave stream the same base tiles at the same time and share
+// them through L2. Each item ends by writing its 128 sorted lists.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "px_common.cuh"
+#include "px_kernels.h"
+#include "px_tc.cuh"
+
+namespace px {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 16;  // tf32 per stage row: 64 bytes = one 64B swizzle span
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 4;
+constexpr int B_BYTES = BN * BK * 4;
+constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+constexpr int kGemmThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr int kNumBars = 2 * STAGES + 2 + 2 + 1;  // full, empty, tmem full, tmem empty, done
+constexpr size_t kGemmSmem = 1024 + STAGES * STAGE_BYTES + kNumBars * 8 + 16;
+
+__device__ __forceinline__ bool mbar_wait_quiet(uint32_t bar, uint32_t parity) {
+  int dummy = 0;
+  return tc::mbar_wait(bar, parity, &dummy);
+}
+
+template <int CAP>
+__device__ __forceinline__ void list_insert(uint64_t (&L)[CAP], uint64_t& thr, int& maxpos,
+                                            uint64_t cand) {
+#pragma unroll
+  for (int j = 0; j < CAP; ++j) L[j] = (j == maxpos) ? cand : L[j];
+  thr = L[0];
+  maxpos = 0;
+#pragma unroll
+  for (int j = 1; j < CAP; ++j) {
+    if (L[j] > thr) {
+      thr = L[j];
+      maxpos = j;
+    }
+  }
+}
+
+template <int CAP>
+__device__ __forceinline__ void list_sort(uint64_t (&L)[CAP]) {
+#pragma unroll
+  for (int size = 2; size <= CAP; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int i = 0; i < CAP; ++i) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool up = (i & size) == 0;
+          const uint64_t a = L[i], b = L[j];
+          const bool sw = up ? (a > b) : (a < b);
+          L[i] = sw ? b : a;
+          L[j] = sw ? a : b;
+        }
+      }
+    }
+  }
+}
+
+template <int CAP, bool L2>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
+                 const __grid_constant__ CUtensorMap tm_xhi, const __grid_constant__ CUtensorMap tm_xlo,
+                 const GemmTopkArgs p) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t smem_base = tc::smem_addr(smem);
+  auto full_bar = [&](int s) { return tc::smem_addr(&bars[s]); };
+  auto empty_bar = [&](int s) { return tc::smem_addr(&bars[STAGES + s]); };
+  auto tfull_bar = [&](int a) { return tc::smem_addr(&bars[2 * STAGES + a]); };
+  auto tempty_bar = [&](int a) { return tc::smem_addr(&bars[2 * STAGES + 2 + a]); };
+  const uint32_t done_bar = tc::smem_addr(&bars[2 * STAGES + 4]);
+
+  const bool q_lo = *p.q_lo_flag != 0;
+  const bool x_lo = p.x_lo_nonzero != 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(full_bar(s), 1);
+      tc::mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(tfull_bar(a), 1);
+      tc::mbar_init(tempty_bar(a), 4);
+    }
+    tc::mbar_init(done_bar, 1);
+    *s_abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tmap(&tm_qhi);
+    tc::prefetch_tmap(&tm_xhi);
+    if (q_lo) tc::prefetch_tmap(&tm_qlo);
+    if (x_lo) tc::prefetch_tmap(&tm_xlo);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tc::smem_addr(s_tmem), kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+
+  const int KC = p.ld / BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_phase[STAGES];
+      bool issued[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) {
+        issued[s] = false;
+        issued_phase[s] = 0;
+      }
+      const uint32_t bytes = A_BYTES + B_BYTES + (q_lo ? A_BYTES : 0) + (x_lo ? B_BYTES : 0);
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+        const int qt = item % p.T;
+        const int split = item / p.T;
+        const int t0 = split * p.tiles_per_split;
+        const int t1 = min(p.nb, t0 + p.tiles_per_split);
+        for (int t = t0; ok && t < t1; ++t) {
+          for (int kc = 0; kc < KC; ++kc) {
+            if (!tc::mbar_wait(empty_bar(stage), phase ^ 1, s_abort)) {
+              ok = false;
+              break;
+            }
+            const uint32_t sbase = smem_base + stage * STAGE_BYTES;
+            tc::mbar_arrive_expect_tx(full_bar(stage), bytes);
+            tc::tma_load_2d(sbase, &tm_qhi, full_bar(stage), kc * BK, qt * BM);
+            if (q_lo) tc::tma_load_2d(sbase + A_BYTES, &tm_qlo, full_bar(stage), kc * BK, qt * BM);
+            tc::tma_load_2d(sbase + 2 * A_BYTES, &tm_xhi, full_bar(stage), kc * BK, t * BN);
+            if (x_lo)
+              tc::tma_load_2d(sbase + 2 * A_BYTES + B_BYTES, &tm_xlo, full_bar(stage), kc * BK, t * BN);
+            issued[stage] = true;
+            issued_phase[stage] = phase;
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
+      }
+      // Every issued load must land before this CTA's shared memory goes away.
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s)
+        if (issued[s]) mbar_wait_quiet(full_bar(s), issued_phase[s]);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_tf32(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+        const int split = item / p.T;
+        const int t0 = split * p.tiles_per_split;
+        const int t1 = min(p.nb, t0 + p.tiles_per_split);
+        for (int t = t0; ok && t < t1; ++t) {
+          if (!tc::mbar_wait(tempty_bar(acc), acc_phase ^ 1, s_abort)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+          for (int kc = 0; kc < KC; ++kc) {
+            if (!tc::mbar_wait(full_bar(stage), phase, s_abort)) {
+              ok = false;
+              break;
+            }
+            tc::tc_fence_after();
+            const uint32_t sbase = smem_base + stage * STAGE_BYTES;
+            const uint64_t a_hi = tc::sw64_kmajor_desc(sbase);
+            const uint64_t a_lo = tc::sw64_kmajor_desc(sbase + A_BYTES);
+            const uint64_t b_hi = tc::sw64_kmajor_desc(sbase + 2 * A_BYTES);
+            const uint64_t b_lo = tc::sw64_kmajor_desc(sbase + 2 * A_BYTES + B_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < BK / 8; ++kk) {
+              const uint64_t off = static_cast<uint64_t>(kk * 32) >> 4;  // 32 bytes per K step
+              const uint32_t accumulate = (kc > 0 || kk > 0) ? 1u : 0u;
+              tc::mma_tf32(d_tmem, a_hi + off, b_hi + off, idesc, accumulate);
+              if (x_lo) tc::mma_tf32(d_tmem, a_hi + off, b_lo + off, idesc, 1u);
+              if (q_lo) tc::mma_tf32(d_tmem, a_lo + off, b_hi + off, idesc, 1u);
+            }
+            tc::mma_commit(empty_bar(stage));
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+          if (!ok) break;
+          tc::mma_commit(tfull_bar(acc));
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1;
+          }
+        }
+      }
+      // All issued MMAs must be complete before TMEM is released.
+      tc::mma_commit(done_bar);
+      mbar_wait_quiet(done_bar, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+      const int qt = item % p.T;
+      const int split = item / p.T;
+      const int t0 = split * p.tiles_per_split;
+      const int t1 = min(p.nb, t0 + p.tiles_per_split);
+      uint64_t L[CAP];
+#pragma unroll
+      for (int j = 0; j < CAP; ++j) L[j] = PX_EMPTY;
+      uint64_t thr = PX_EMPTY;
+      float thr_key = __int_as_float(0x7f800000);  // +inf: accept everything at first
+      int maxpos = 0;
+      for (int t = t0; t < t1; ++t) {
+        // Warp-uniform decision: the tcgen05.ld below is .sync.aligned.
+        const bool got = __all_sync(0xffffffffu, tc::mbar_wait(tfull_bar(acc), acc_phase, s_abort));
+        if (!got) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const int64_t row0 = static_cast<int64_t>(t) * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tc::tmem_ld_32x32b_x32(lane_addr + static_cast<uint32_t>(acc * BN + c * 32), v);
+          tc::tmem_ld_wait();
+          const int64_t rbase = row0 + c * 32;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int64_t row = rbase + j;
+            if (row < p.n) {
+              const float dot = __uint_as_float(v[j]);
+              const float key = L2 ? fmaf(-2.0f, dot, __ldg(p.norms + row)) : -dot;
+              if (key <= thr_key) {
+                const uint64_t cand = pack_cand(key, static_cast<uint32_t>(row));
+                if (cand < thr) {
+                  list_insert<CAP>(L, thr, maxpos, cand);
+                  thr_key = thr == PX_EMPTY ? __int_as_float(0x7f800000) : cand_key(thr);
+                }
+              }
+            }
+          }
+        }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(tempty_bar(acc));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      list_sort<CAP>(L);
+      const int64_t qidx = static_cast<int64_t>(qt) * BM + row_in_tile;
+      if (qidx < p.nq) {
+        uint64_t* out = p.partial + (qidx * p.S + split) * CAP;
+#pragma unroll
+        for (int j = 0; j < CAP; ++j) out[j] = L[j];
+      }
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  if (warp == 1) tc::tmem_dealloc(tmem_base, kTmemCols);
+  if (threadIdx.x == 0 && *s_abort) atomicOr(p.err, 1);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+template <int CAP, bool L2>
+cudaError_t launch_typed(const GemmTopkArgs& a, const CUtensorMap* maps, int grid, cudaStream_t stream) {
+  auto kern = gemm_topk_kernel<CAP, L2>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kGemmSmem));
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kGemmThreads, kGemmSmem, stream>>>(maps[0], maps[1], maps[2], maps[3], a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// A [rows x ld] fp32 plane as a TMA tensor: boxes of BK (64 bytes) x box_rows,
+// 64-byte swizzle, out-of-range rows read as zeros.
+cudaError_t encode_plane_map(CUtensorMap* map, const float* plane, int64_t rows, int ld, int box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = get_encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if (rows < 1) rows = 1;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(ld), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * sizeof(float)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(plane), dims, strides, box,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+int gemm_cap_for(int k) {
+  if (k <= 16) return 32;
+  if (k <= 40) return 64;
+  return 0;
+}
+
+size_t gemm_smem_bytes() { return kGemmSmem; }
+
+cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const float* q_hi, const float* q_lo,
+                             int64_t q_rows, const float* x_hi, const float* x_lo, int grid,
+                             cudaStream_t stream) {
+  if (a.ld % BK != 0) return cudaErrorInvalidValue;
+  CUtensorMap maps[4];
+  cudaError_t e = encode_plane_map(&maps[0], q_hi, q_rows, a.ld, BM);
+  if (e == cudaSuccess) e = encode_plane_map(&maps[1], q_lo, q_rows, a.ld, BM);
+  if (e == cudaSuccess) e = encode_plane_map(&maps[2], x_hi, a.n, a.ld, BN);
+  if (e == cudaSuccess) e = encode_plane_map(&maps[3], x_lo, a.n, a.ld, BN);
+  if (e != cudaSuccess) return e;
+  const int cap = gemm_cap_for(a.k);
+  if (cap == 32) return a.l2 ? launch_typed<32, true>(a, maps, grid, stream)
+                             : launch_typed<32, false>(a, maps, grid, stream);
+  if (cap == 64) return a.l2 ? launch_typed<64, true>(a, maps, grid, stream)
+                             : launch_typed<64, false>(a, maps, grid, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace px

@@ -24,7 +24,7 @@ __device__ __forceinline__ float tf32_rn(float x) {
 __global__ void prepare_rows_kernel(const float* __restrict__ src, int64_t n, int d, int ld,
                                     float* __restrict__ dst, float* __restrict__ hi,
                                     float* __restrict__ lo, float* __restrict__ norms,
-                                    int* __restrict__ lo_nonzero) {
+                                    int* __restrict__ lo_nonzero, int* __restrict__ max_norm_sq) {
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= n) return;
@@ -43,7 +43,7 @@ __global__ void prepare_rows_kernel(const float* __restrict__ src, int64_t n, in
   __syncwarp();
   const bool any_nz = __any_sync(0xffffffffu, nz);
   if (lo_nonzero && any_nz && lane == 0) atomicOr(lo_nonzero, 1);
-  if (norms && lane == 0) {
+  if ((norms || max_norm_sq) && lane == 0) {
     // Squared norm in the reference's 8-lane order (l2_sqr(x, 0)).
     const float* x = (dst ? dst + row * ld : src + row * d);
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -55,7 +55,8 @@ __global__ void prepare_rows_kernel(const float* __restrict__ src, int64_t n, in
 #pragma unroll
     for (int l = 1; l < 8; ++l) s = __fadd_rn(s, acc[l]);
     for (int i = chunks * 8; i < d; ++i) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
-    norms[row] = s;
+    if (norms) norms[row] = s;
+    if (max_norm_sq) atomicMax(max_norm_sq, __float_as_int(s));  // s >= 0: int order = float order
   }
 }
 
@@ -67,19 +68,20 @@ __global__ void zero_rows_kernel(float* __restrict__ p, int64_t begin, int64_t e
 }  // namespace
 
 cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, float* dst, float* hi,
-                                float* lo, float* norms, int* lo_nonzero, cudaStream_t stream) {
+                                float* lo, float* norms, int* lo_nonzero, int* max_norm_sq,
+                                cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
   const int threads = 256;
   const int64_t blocks = (n * 32 + threads - 1) / threads;
-  prepare_rows_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(src, n, d, ld, dst, hi,
-                                                                          lo, norms, lo_nonzero);
+  prepare_rows_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+      src, n, d, ld, dst, hi, lo, norms, lo_nonzero, max_norm_sq);
   return cudaGetLastError();
 }
 
 cudaError_t launch_split_queries(const float* q, int64_t nq, int d, int ld, int64_t rows_alloc,
                                  float* hi, float* lo, float* norms, int* lo_nonzero,
                                  cudaStream_t stream) {
-  cudaError_t e = launch_prepare_rows(q, nq, d, ld, nullptr, hi, lo, norms, lo_nonzero, stream);
+  cudaError_t e = launch_prepare_rows(q, nq, d, ld, nullptr, hi, lo, norms, lo_nonzero, nullptr, stream);
   if (e != cudaSuccess) return e;
   if (rows_alloc > nq) {
     const int64_t count = (rows_alloc - nq) * ld;

@@ -1,0 +1,168 @@
+// K5: exact rescoring and certification of tensor-core candidates.
+//
+// Input: per query the CAP best candidates by the approximate key of the
+// tensor-core pass, merged over all splits and sorted. Each candidate is
+// rescored with the reference's exact arithmetic (distance.rs:4-39 via
+// exact_key), the CAP exact keys are ranked (ties by row), and the first k
+// are the answer -- provided no row outside the candidate set can beat the
+// k-th. That is certified with a rigorous bound eps on |approx - exact|:
+//   every non-candidate x has approx(x) >= A, the largest approximate key
+//   among the candidates, hence exact(x) >= A - eps; the result is exact if
+//   exact_k < A - eps (strict, so no outside row can even tie).
+// A query whose certificate fails is listed for the exact streaming scan.
+//
+// eps is a worst-case bound, in double precision, built from
+//   S = ||q|| * max_x ||x|| >= sum_i |q_i x_i|        (Cauchy-Schwarz)
+// the tf32 split error (4 * 2^-22 * S when a lo plane is in use), an
+// allowance of 2 * 2^-22 * S per tensor-core accumulation step, and the
+// rounding of the reference arithmetic and of the norms.
+#include "px_common.cuh"
+#include "px_kernels.h"
+
+namespace px {
+
+namespace {
+
+constexpr int kRescoreWarps = 4;
+
+template <bool L2>
+__global__ void __launch_bounds__(kRescoreWarps * 32)
+rescore_kernel(const RescoreArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int dq = (a.d + 3) & ~3;
+  float* s_q = reinterpret_cast<float*>(smem_raw) + warp * dq;
+  uint64_t* s_c = reinterpret_cast<uint64_t*>(reinterpret_cast<float*>(smem_raw) + kRescoreWarps * dq) +
+                  warp * 2 * 64;
+  uint64_t* s_sorted = s_c + 64;
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * kRescoreWarps + warp;
+  if (q >= a.nq) return;
+
+  const float* qv = a.queries + q * a.d;
+  double qsq = 0.0;
+  for (int i = lane; i < a.d; i += 32) {
+    const float v = qv[i];
+    s_q[i] = v;
+    qsq += static_cast<double>(v) * v;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) qsq += __shfl_xor_sync(0xffffffffu, qsq, off);
+  __syncwarp();
+
+  const uint64_t* mq = a.merged + q * a.cap;
+  for (int j = lane; j < a.cap; j += 32) {
+    const uint64_t c = mq[j];
+    uint64_t e = PX_EMPTY;
+    if (c != PX_EMPTY) {
+      const uint32_t row = cand_row(c);
+      const float key = exact_key<L2>(s_q, a.base + static_cast<int64_t>(row) * a.ld, a.d);
+      e = pack_cand(key, row);
+    }
+    s_c[j] = e;
+  }
+  __syncwarp();
+  // Rank sort (values are distinct except PX_EMPTY; equal ones rank by index).
+  for (int j = lane; j < a.cap; j += 32) {
+    const uint64_t v = s_c[j];
+    int rank = 0;
+    for (int i = 0; i < a.cap; ++i) {
+      const uint64_t u = s_c[i];
+      rank += (u < v) || (u == v && i < j);
+    }
+    s_sorted[rank] = v;
+  }
+  __syncwarp();
+
+  // Certificate.
+  int ok = 1;
+  const uint64_t last = mq[a.cap - 1];
+  const uint64_t kth = s_sorted[a.k - 1];
+  if (last != PX_EMPTY && kth != PX_EMPTY) {
+    const double qn = sqrt(qsq);
+    const double xn = static_cast<double>(a.max_norm);
+    const bool q_lo = *a.q_lo_flag != 0;
+    const int npass = 1 + (q_lo ? 1 : 0) + (a.x_lo_nonzero ? 1 : 0);
+    const double rep = (q_lo || a.x_lo_nonzero) ? 4.0 * 0x1p-22 : 0.0;
+    const double steps = static_cast<double>(npass) * ((a.d + 7) / 8) + 2.0;
+    const double S = qn * xn;
+    const double e_dot = S * (rep + 2.0 * steps * 0x1p-22);
+    const double ref = (a.d / 8 + 10) * 0x1p-23;
+    const double A = static_cast<double>(cand_key(last));
+    const double Ek = static_cast<double>(cand_key(kth));
+    double bound;
+    if (L2) {
+      const double qn2 = qn * qn;
+      const double eps = 2.0 * e_dot + xn * xn * ref + (qn + xn) * (qn + xn) * ref +
+                         (fabs(A) + qn2) * 0x1p-22;
+      bound = A + qn2 - eps;
+    } else {
+      const double eps = e_dot + S * ref + fabs(A) * 0x1p-22;
+      bound = A - eps;
+    }
+    ok = Ek < bound ? 1 : 0;
+  }
+  for (int j = lane; j < a.k; j += 32) a.out[q * a.k + j] = s_sorted[j];
+  if (lane == 0) {
+    a.status[q] = ok ? 0 : 1;
+    if (!ok) {
+      const int pos = atomicAdd(a.n_fail, 1);
+      a.fail_list[pos] = static_cast<int>(q);
+    }
+  }
+}
+
+__global__ void gather_rows_kernel(const float* __restrict__ src, int d, const int* __restrict__ idx,
+                                   int count, float* __restrict__ dst) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(count) * d) return;
+  const int r = static_cast<int>(i / d), e = static_cast<int>(i - static_cast<int64_t>(r) * d);
+  dst[i] = src[static_cast<int64_t>(idx[r]) * d + e];
+}
+
+__global__ void scatter_cands_kernel(const uint64_t* __restrict__ src, int k, const int* __restrict__ idx,
+                                     int count, uint64_t* __restrict__ dst) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(count) * k) return;
+  const int r = static_cast<int>(i / k), j = static_cast<int>(i - static_cast<int64_t>(r) * k);
+  dst[static_cast<int64_t>(idx[r]) * k + j] = src[i];
+}
+
+}  // namespace
+
+cudaError_t launch_rescore(const RescoreArgs& a, cudaStream_t stream) {
+  if (a.nq == 0) return cudaSuccess;
+  if (a.cap > 64 || a.k > a.cap) return cudaErrorInvalidValue;
+  const int dq = (a.d + 3) & ~3;
+  const size_t smem = sizeof(float) * kRescoreWarps * dq + sizeof(uint64_t) * kRescoreWarps * 128;
+  const unsigned blocks = static_cast<unsigned>((a.nq + kRescoreWarps - 1) / kRescoreWarps);
+  if (a.l2) {
+    cudaError_t e = cudaFuncSetAttribute(rescore_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    rescore_kernel<true><<<blocks, kRescoreWarps * 32, smem, stream>>>(a);
+  } else {
+    cudaError_t e = cudaFuncSetAttribute(rescore_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    rescore_kernel<false><<<blocks, kRescoreWarps * 32, smem, stream>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(const float* src, int d, const int* idx, int count, float* dst,
+                               cudaStream_t stream) {
+  const int64_t total = static_cast<int64_t>(count) * d;
+  if (total == 0) return cudaSuccess;
+  gather_rows_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(src, d, idx, count, dst);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scatter_cands(const uint64_t* src, int k, const int* idx, int count, uint64_t* dst,
+                                 cudaStream_t stream) {
+  const int64_t total = static_cast<int64_t>(count) * k;
+  if (total == 0) return cudaSuccess;
+  scatter_cands_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(src, k, idx, count, dst);
+  return cudaGetLastError();
+}
+
+}  // namespace px

@@ -225,6 +225,10 @@ void FlatShard::release() {
   x = hi = lo = norms = nullptr;
   if (flag) cudaFree(flag);
   flag = nullptr;
+  if (ev_start) cudaEventDestroy(ev_start);
+  if (ev_stop) cudaEventDestroy(ev_stop);
+  ev_start = ev_stop = nullptr;
+  fb.release();
   ws.release();
   stage.release();
   segs.dev.release();
@@ -238,7 +242,7 @@ px_status FlatShard::append_device(const float* d_src, int64_t count, int d, int
   px_status s = ensure_capacity(n + count, ld);
   if (s != PX_OK) return s;
   cudaError_t e = launch_prepare_rows(d_src, count, d, ld, x + n * ld, hi + n * ld, lo + n * ld,
-                                      norms + n, flag, stream);
+                                      norms + n, flag, flag + 2, stream);
   if (e != cudaSuccess) return cuda_status(e, "prepare_rows launch");
   segs.local.push_back(n);
   segs.global.push_back(global_begin);
@@ -246,10 +250,12 @@ px_status FlatShard::append_device(const float* d_src, int64_t count, int d, int
   n += count;
   e = cudaStreamSynchronize(stream);
   if (e != cudaSuccess) return cuda_status(e, "add");
-  int h_flag = 0;
-  e = cudaMemcpy(&h_flag, flag, sizeof(int), cudaMemcpyDeviceToHost);
+  int h_flag[4] = {0, 0, 0, 0};
+  e = cudaMemcpy(h_flag, flag, sizeof(h_flag), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_status(e, "add flag readback");
-  lo_nonzero = h_flag != 0;
+  lo_nonzero = h_flag[0] != 0;
+  std::memcpy(&max_norm_sq, &h_flag[2], sizeof(float));
+  g_launches += 1;
   return PX_OK;
 }
 
@@ -294,6 +300,8 @@ PX_API px_status px_flat_create(int32_t dim, int32_t metric, const int32_t* devi
     cudaError_t e = cudaStreamCreateWithFlags(&sh.stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&sh.flag, 4 * sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(sh.flag, 0, 4 * sizeof(int));
+    if (e == cudaSuccess) e = cudaEventCreate(&sh.ev_start);
+    if (e == cudaSuccess) e = cudaEventCreate(&sh.ev_stop);
     if (e != cudaSuccess) {
       px_status st = cuda_status(e, "create");
       for (auto& x : h->shards) x.release();
@@ -320,6 +328,41 @@ PX_API px_status px_flat_destroy(px_flat* h) {
 PX_API int64_t px_flat_size(const px_flat* h) { return h ? h->total : 0; }
 PX_API int32_t px_flat_dim(const px_flat* h) { return h ? h->dim : 0; }
 PX_API int32_t px_flat_metric(const px_flat* h) { return h ? h->metric : -1; }
+
+PX_API px_status px_flat_set_path(px_flat* h, int32_t mode) {
+  px_status s = flat_check(h);
+  if (s != PX_OK) return s;
+  if (mode != PX_PATH_AUTO && mode != PX_PATH_EXACT && mode != PX_PATH_TENSOR)
+    return set_error(PX_EINVAL, "path mode must be PX_PATH_AUTO, PX_PATH_EXACT or PX_PATH_TENSOR");
+  h->path_mode = mode;
+  return PX_OK;
+}
+
+PX_API void px_set_profiling(int32_t enable) { g_profiling = enable ? 1 : 0; }
+
+PX_API int64_t px_launch_count(void) { return g_launches.load(); }
+
+PX_API px_status px_flat_last_profile(const px_flat* h, px_search_profile* out) {
+  px_status s = flat_check(h);
+  if (s != PX_OK) return s;
+  if (out == nullptr) return set_error(PX_EINVAL, "out is null");
+  const FlatShard& sh = h->shards[0];
+  out->path = sh.last_path;
+  out->launches = sh.last_launches;
+  out->fallback_queries = sh.last_fallback;
+  out->profiled = 0;
+  out->main_kernel_ms = 0.f;
+  if (sh.last_profiled) {
+    DeviceGuard dg(sh.device);
+    float ms = 0.f;
+    cudaError_t e = cudaEventSynchronize(sh.ev_stop);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, sh.ev_start, sh.ev_stop);
+    if (e != cudaSuccess) return cuda_status(e, "profile events");
+    out->profiled = 1;
+    out->main_kernel_ms = ms;
+  }
+  return PX_OK;
+}
 
 PX_API px_status px_flat_set_id_offset(px_flat* h, int64_t offset) {
   px_status s = flat_check(h);
@@ -389,7 +432,7 @@ static px_status shard_search(const px_flat* h, FlatShard& sh, int metric, const
   px_status s = sh.segs.sync_device();
   if (s != PX_OK) return s;
   SearchPlan plan;
-  s = plan_flat_search(h, sh, nq, k, plan);
+  s = plan_flat_search(h, sh, nq, k, d_mask != nullptr, plan);
   if (s != PX_OK) return s;
   cudaError_t e = sh.ws.reserve(plan.ws_bytes);
   if (e != cudaSuccess) return cuda_status(e, "search workspace allocation");
@@ -398,6 +441,8 @@ static px_status shard_search(const px_flat* h, FlatShard& sh, int metric, const
   e = launch_emit(plan.final_cands, nq, k, l2, natural, sh.segs.view(h->id_offset), d_ids, d_dists,
                   stream);
   if (e != cudaSuccess) return cuda_status(e, "emit launch");
+  g_launches += 1;
+  sh.last_launches += 1;
   return PX_OK;
 }
 

@@ -88,12 +88,63 @@ cudaError_t launch_nearest_centroid(const float* vectors, int64_t n, int m, int 
 
 // ---- shard preparation (k_prep.cu) ----------------------------------------
 // Copies n rows of d floats into the shard (stride ld, zero padded), and
-// writes the tf32 hi/lo split planes and the squared norms.
+// writes the tf32 hi/lo split planes and the squared norms. lo_nonzero is
+// raised when any lo element is nonzero; max_norm_sq (float bits) is raised
+// to the largest squared norm.
 cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, float* dst,
                                 float* hi, float* lo, float* norms, int* lo_nonzero,
-                                cudaStream_t stream);
+                                int* max_norm_sq, cudaStream_t stream);
 cudaError_t launch_split_queries(const float* q, int64_t nq, int d, int ld, int64_t rows_alloc,
                                  float* hi, float* lo, float* norms, int* lo_nonzero,
                                  cudaStream_t stream);
+
+// ---- K1: tensor-core candidate generation (k_gemm.cu) ---------------------
+struct GemmTopkArgs {
+  int nq;
+  int64_t n;            // shard rows
+  int ld;               // row stride (floats), multiple of 16
+  int k;
+  int T;                // query tiles of 128
+  int S;                // base splits
+  int tiles_per_split;  // base tiles of 256 rows per split
+  int nb;               // base tiles
+  int n_items;          // T * S
+  bool l2;
+  const float* norms;   // squared norms (L2)
+  int x_lo_nonzero;     // shard lo plane in use
+  const int* q_lo_flag; // device word: query lo plane in use
+  uint64_t* partial;    // [nq][S][cap] sorted approximate candidates
+  int* err;             // device word raised on a timed-out wait
+};
+int gemm_cap_for(int k);  // candidates kept per query (0: k unsupported)
+size_t gemm_smem_bytes();
+cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const float* q_hi, const float* q_lo,
+                             int64_t q_rows, const float* x_hi, const float* x_lo, int grid,
+                             cudaStream_t stream);
+
+// ---- K5: exact rescoring + certificate (k_rescore.cu) ---------------------
+struct RescoreArgs {
+  const uint64_t* merged;  // [nq][cap] sorted approximate candidates
+  int64_t nq;
+  int cap;
+  int k;
+  const float* queries;    // nq x d
+  const float* base;       // shard fp32 rows, stride ld
+  int ld;
+  int d;
+  bool l2;
+  float max_norm;          // max ||x|| over the shard
+  int x_lo_nonzero;
+  const int* q_lo_flag;
+  uint64_t* out;           // [nq][k] exact candidates
+  int* status;             // [nq] 0 = certified
+  int* n_fail;             // count of uncertified queries
+  int* fail_list;          // their indices
+};
+cudaError_t launch_rescore(const RescoreArgs& a, cudaStream_t stream);
+cudaError_t launch_gather_rows(const float* src, int d, const int* idx, int count, float* dst,
+                               cudaStream_t stream);
+cudaError_t launch_scatter_cands(const uint64_t* src, int k, const int* idx, int count,
+                                 uint64_t* dst, cudaStream_t stream);
 
 }  // namespace px

@@ -1,6 +1,7 @@
 // Host-side runtime structures shared by the C ABI translation units.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <mutex>
 #include <string>
@@ -65,11 +66,16 @@ struct FlatShard {
   float* lo = nullptr;     // tf32(x - hi)
   float* norms = nullptr;  // squared norms
   int64_t n = 0, cap = 0;
-  int* flag = nullptr;     // [0] lo plane nonzero, [1] device error code
+  int* flag = nullptr;     // [0] lo plane nonzero, [1] device error code, [2] max squared norm (bits)
   bool lo_nonzero = false;
+  float max_norm_sq = 0.f;
+  cudaEvent_t ev_start = nullptr, ev_stop = nullptr;  // brackets the dominant kernel when profiling
+  int last_path = 0, last_fallback = 0, last_launches = 0;
+  bool last_profiled = false;
   px::Segments segs;
   px::DevBuf ws;           // search workspace
   px::DevBuf stage;        // uploads (queries, rows, masks, outputs)
+  px::DevBuf fb;           // certificate-fallback workspace
   int64_t* out_ids = nullptr;  // results of the last search (inside stage)
   float* out_dists = nullptr;
 
@@ -97,6 +103,7 @@ struct px_flat {
   int metric = 0;
   int64_t total = 0;
   int64_t id_offset = 0;
+  int path_mode = PX_PATH_AUTO;
   std::vector<FlatShard> shards;
   GatherBuf gather;
   std::mutex mu;
@@ -108,15 +115,23 @@ enum class FlatPath { Exact = 0, Gemm = 1 };
 
 struct SearchPlan {
   FlatPath path = FlatPath::Exact;
+  // exact scan
   int group = 1;
   int ncta = 1;
   int64_t rows_per_cta = 0;
+  // tensor-core path
+  int cap = 0, T = 0, S = 0, nb = 0, tiles_per_split = 0, n_items = 0, grid = 0;
+  int64_t q_rows = 0;
   size_t ws_bytes = 0;
   uint64_t* partial = nullptr;
   uint64_t* final_cands = nullptr;
 };
 
-px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, int k, SearchPlan& plan);
+extern std::atomic<int64_t> g_launches;
+extern std::atomic<int> g_profiling;
+
+px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, int k, bool masked,
+                           SearchPlan& plan);
 px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int metric,
                           const float* d_q, int64_t nq, int k, const uint8_t* d_mask,
                           cudaStream_t stream);

@@ -258,3 +258,69 @@ def test_multi_device_handle_if_available(pxm):
     idx.add(data[5000:])
     ids, d = idx.search_batch(queries, k=10)
     _parity.check_flat(data, O.L2, queries, ids, d, 10)
+
+
+# ---- the tensor-core path (K1 tcgen05 3xTF32 + K5 exact rescoring) --------
+
+def _run_path(pxm, data, metric, queries, k, path):
+    idx = pxm.FlatIndex(data.shape[1], _metric(pxm, metric))
+    idx.add(data)
+    idx.set_search_path(path)
+    ids, d = idx.search_batch(queries, k=k)
+    return ids, d, idx.last_search_profile()
+
+
+@pytest.mark.parametrize("metric", [O.L2, O.IP])
+@pytest.mark.parametrize("n,dim,nq,k", [
+    (5000, 32, 16, 10), (20000, 64, 128, 10), (9000, 128, 300, 16), (12345, 24, 77, 1),
+    (30000, 96, 200, 40), (8192, 768, 130, 10), (4096, 384, 129, 5),
+])
+def test_tensor_path_parity(pxm, metric, n, dim, nq, k):
+    data = _data.unit_gaussian(n, dim, n + dim) if metric == O.IP else \
+        _data.gaussian_mixture(n, nq, d=dim, centres=50, seed=dim)[0]
+    queries = _data.unit_gaussian(nq, dim, 7 * dim) if metric == O.IP else \
+        _data.gaussian_mixture(10, nq, d=dim, centres=50, seed=dim)[1]
+    ids, d, prof = _run_path(pxm, data, metric, queries, k, "tensor")
+    assert prof["path"] == "tensor"
+    _parity.check_flat(data, metric, queries, ids, d, k)
+    # Fallbacks are legal but must stay rare on generic data.
+    assert prof["fallback_queries"] <= max(2, nq // 20), prof
+
+
+def test_tensor_path_integer_data_single_pass(pxm):
+    # Config 2's integer data: the tf32 lo planes are zero, one MMA pass is exact.
+    data, queries = _data.sift_like(40000, 64, seed=11, centres=100)
+    ids, d, prof = _run_path(pxm, data, O.L2, queries, 10, "tensor")
+    _parity.check_flat(data, O.L2, queries, ids, d, 10)
+
+
+def test_tensor_path_certificate_fallback_on_ties(pxm):
+    # Every row appears 40 times: ties exceed the candidate capacity, the
+    # certificate cannot hold, and the exact scan must take over.
+    base = _data.unit_gaussian(300, 64, 3)
+    data = np.repeat(base, 40, axis=0)
+    queries = _data.unit_gaussian(32, 64, 4)
+    ids, d, prof = _run_path(pxm, data, O.IP, queries, 10, "tensor")
+    assert prof["fallback_queries"] > 0
+    _parity.check_flat(data, O.IP, queries, ids, d, 10)
+
+
+def test_auto_path_uses_tensor_cores_for_batches(pxm):
+    data = _data.unit_gaussian(20000, 128, 9)
+    queries = _data.unit_gaussian(64, 128, 10)
+    idx = pxm.FlatIndex(128, pxm.Metric.InnerProduct)
+    idx.add(data)
+    ids, d = idx.search_batch(queries, k=10)
+    assert idx.last_search_profile()["path"] == "tensor"
+    _parity.check_flat(data, O.IP, queries, ids, d, 10)
+    ids1, d1 = idx.search(queries[5], k=10)
+    assert idx.last_search_profile()["path"] == "exact"
+    assert ids1.tolist() == ids[5].tolist()
+
+
+def test_tensor_path_rejects_what_it_cannot_serve(pxm):
+    idx = pxm.FlatIndex(16, pxm.Metric.L2)
+    idx.add(O.gen_uniform(5000, 16, 1))
+    idx.set_search_path("tensor")
+    with pytest.raises(pxm.PxError):
+        idx.search_batch(O.gen_uniform(32, 16, 2), k=41)
