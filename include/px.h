@@ -94,6 +94,10 @@ PX_API px_status px_flat_add(px_flat* h, const float* rows, int64_t n);
  * device (handles with ndev == 1 only). Rows are not checked for NaN/Inf. */
 PX_API px_status px_flat_add_device(px_flat* h, const float* d_rows, int64_t n);
 
+/* Pre-sizes every shard for `n_total` rows in all (split as px_flat_add
+ * splits), so that later adds up to that size do not reallocate. */
+PX_API px_status px_flat_reserve(px_flat* h, int64_t n_total);
+
 PX_API int64_t px_flat_size(const px_flat* h);
 PX_API int32_t px_flat_dim(const px_flat* h);
 PX_API int32_t px_flat_metric(const px_flat* h);

@@ -112,6 +112,10 @@ class FlatIndex:
         _check_finite(v)
         _lib.check(self._lib.px_flat_add(self._h, _ptr(v, _f32p), v.shape[0]))
 
+    def reserve(self, n_total: int) -> None:
+        """Pre-sizes device storage for n_total rows (no reallocation on add)."""
+        _lib.check(self._lib.px_flat_reserve(self._h, _usize(n_total, "n_total")))
+
     def _search(self, q: np.ndarray, nq: int, k: int, mask=None):
         ids = np.zeros((nq, k), dtype=np.int64)
         dists = np.zeros((nq, k), dtype=np.float32)

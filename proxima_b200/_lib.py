@@ -59,6 +59,7 @@ SIGNATURES = {
     "px_flat_destroy": (_i32, [_vp]),
     "px_flat_add": (_i32, [_vp, _f32p, _i64]),
     "px_flat_add_device": (_i32, [_vp, _vp, _i64]),
+    "px_flat_reserve": (_i32, [_vp, _i64]),
     "px_flat_size": (_i64, [_vp]),
     "px_flat_dim": (_i32, [_vp]),
     "px_flat_metric": (_i32, [_vp]),

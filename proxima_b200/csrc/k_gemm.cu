@@ -46,7 +46,7 @@ constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
 constexpr int kGemmThreads = 192;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kNumBars = 2 * STAGES + 2 + 2 + 1;  // full, empty, tmem full, tmem empty, done
-constexpr size_t kGemmSmem = 1024 + STAGES * STAGE_BYTES + kNumBars * 8 + 16;
+constexpr size_t kGemmSmem = 1024 + STAGES * STAGE_BYTES + kNumBars * 8 + 16 + BM * 33 * 4;
 
 __device__ __forceinline__ bool mbar_wait_quiet(uint32_t bar, uint32_t parity) {
   int dummy = 0;
@@ -101,6 +101,7 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+  float* s_keys = reinterpret_cast<float*>(s_tmem + 4);  // 128 x 33 epilogue key slots
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -275,20 +276,48 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
         }
         tc::tc_fence_after();
         const int64_t row0 = static_cast<int64_t>(t) * BN;
+        // Columns of this tile that are real rows (the last tile may be short).
+        const int valid_cols = p.n - row0 < BN ? static_cast<int>(p.n - row0) : BN;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t v[32];
           tc::tmem_ld_32x32b_x32(lane_addr + static_cast<uint32_t>(acc * BN + c * 32), v);
           tc::tmem_ld_wait();
           const int64_t rbase = row0 + c * 32;
+          const int nvalid = valid_cols - c * 32;
+          if (nvalid <= 0) continue;
+          // Hot path: keys and a bit mask of those that beat the threshold.
+          float key[32];
+          if (L2) {
+            const float4* nrm = reinterpret_cast<const float4*>(p.norms + rbase);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int64_t row = rbase + j;
-            if (row < p.n) {
-              const float dot = __uint_as_float(v[j]);
-              const float key = L2 ? fmaf(-2.0f, dot, __ldg(p.norms + row)) : -dot;
-              if (key <= thr_key) {
-                const uint64_t cand = pack_cand(key, static_cast<uint32_t>(row));
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 nv = __ldg(nrm + j4);
+              key[4 * j4 + 0] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 0]), nv.x);
+              key[4 * j4 + 1] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 1]), nv.y);
+              key[4 * j4 + 2] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 2]), nv.z);
+              key[4 * j4 + 3] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 3]), nv.w);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) key[j] = -__uint_as_float(v[j]);
+          }
+          uint32_t pass = 0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) pass |= (key[j] <= thr_key ? 1u : 0u) << j;
+          if (nvalid < 32) pass &= (1u << nvalid) - 1u;
+          if (pass) {
+            // Rare path, one copy of the insertion code: keys go through
+            // this thread's shared-memory slot so they can be indexed.
+            float* slot = s_keys + row_in_tile * 33;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) slot[j] = key[j];
+            while (pass) {
+              const int j = __ffs(pass) - 1;
+              pass &= pass - 1;
+              const float kj = slot[j];
+              if (kj <= thr_key) {
+                const uint64_t cand = pack_cand(kj, static_cast<uint32_t>(rbase + j));
                 if (cand < thr) {
                   list_insert<CAP>(L, thr, maxpos, cand);
                   thr_key = thr == PX_EMPTY ? __int_as_float(0x7f800000) : cand_key(thr);

@@ -184,7 +184,11 @@ px_status FlatShard::ensure_capacity(int64_t need, int ld) {
   cudaError_t e = cudaMalloc(&nx, pb);
   if (e == cudaSuccess) e = cudaMalloc(&nhi, pb);
   if (e == cudaSuccess) e = cudaMalloc(&nlo, pb);
-  if (e == cudaSuccess) e = cudaMalloc(&nn, sizeof(float) * new_cap);
+  // Norms are padded to a whole number of 256-row tiles: the tensor-core
+  // epilogue reads them 32 rows at a time, past the last row of a shard.
+  const int64_t norm_cap = (new_cap + 255) / 256 * 256;
+  if (e == cudaSuccess) e = cudaMalloc(&nn, sizeof(float) * norm_cap);
+  if (e == cudaSuccess) e = cudaMemset(nn, 0, sizeof(float) * norm_cap);
   if (e != cudaSuccess) {
     cudaGetLastError();
     if (nx) cudaFree(nx);
@@ -402,6 +406,22 @@ PX_API px_status px_flat_add(px_flat* h, const float* rows, int64_t n) {
     if (s != PX_OK) return s;
   }
   h->total += n;
+  return PX_OK;
+}
+
+PX_API px_status px_flat_reserve(px_flat* h, int64_t n_total) {
+  px_status s = flat_check(h);
+  if (s != PX_OK) return s;
+  if (n_total < 0) return set_error(PX_EINVAL, "row count must be >= 0");
+  std::lock_guard<std::mutex> lk(h->mu);
+  const int64_t G = static_cast<int64_t>(h->shards.size());
+  const int64_t per = (n_total + G - 1) / G;
+  for (auto& sh : h->shards) {
+    if (per > 0xFFFFFFFFll) return set_error(PX_EUNSUPPORTED, "a shard holds at most 2^32-1 rows");
+    DeviceGuard dg(sh.device);
+    s = sh.ensure_capacity(std::max(per, sh.n), h->ld);
+    if (s != PX_OK) return s;
+  }
   return PX_OK;
 }
 
