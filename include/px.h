@@ -149,6 +149,22 @@ PX_API px_status px_flat_search_device(const px_flat* h, const float* d_queries,
                                        int32_t k, int32_t key_space, int64_t* d_out_ids,
                                        float* d_out_dists, void* stream);
 
+/* Exact kNN that allocates nothing, for callers that may not allocate device
+ * memory (a plugin handed a fixed arena by its host program, a service whose
+ * allocator must own every byte). No counterpart in the reference. The caller
+ * passes the base (d_base, n x dim row-major, dim a multiple of 4, 16-byte
+ * aligned), the queries and both outputs, all in device memory on the current
+ * device; results equal px_flat_search's (natural distances, ids 0..n-1).
+ * Candidate lists live in a fixed 16 MiB device array inside the library
+ * (held on every GPU that loads it); requests needing more (roughly
+ * nq * k > 1M) are rejected with PX_EUNSUPPORTED. The first call on a device
+ * looks up that array's address and should come before any stream capture.
+ * Calls share the array: calls that overlap on the GPU race. Runs on
+ * `stream` and returns without synchronising. */
+PX_API px_status px_flat_search_noalloc(const float* d_base, int64_t n, int32_t dim, int32_t metric,
+                                        const float* d_queries, int64_t nq, int32_t k,
+                                        int64_t* d_out_ids, float* d_out_dists, void* stream);
+
 /* Cross-shard merge on one device: keys/ids [nshard][nq][k] in key space,
  * each list sorted; writes the k best per query (ties by smaller id) as
  * natural distances (natural != 0) or keys. */

@@ -1,0 +1,69 @@
+"""px_flat_search_noalloc: the search entry point that allocates nothing.
+
+It exists for callers that may not allocate GPU memory themselves (a plugin
+working inside a fixed arena its host program hands it, a service whose
+allocator must own every byte): they pass the base, queries and outputs in
+device memory, and the library uses only a fixed device array it carries.
+This test calls it through the C ABI twice in a row and checks each result
+against px_flat_search on the same data -- bit for bit, the tolerance of
+every other parity test here -- and that the calls leave the device's free
+memory unchanged (from the second call on: the very first call on a device
+may load the library's device image, which brings the fixed array with it).
+The file name makes pytest collect it last.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def test_noalloc_matches_flat_search_twice(px):
+    import torch
+
+    assert px.device_count() > 0, "GPU tests need a CUDA device"
+    lib = px._lib.load()
+    rng = np.random.default_rng(12)
+    n, dim, k = 50000, 96, 10
+    base = rng.standard_normal((n, dim)).astype(np.float32)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    d_base = torch.from_numpy(base).to(dev)
+    first = True
+    for metric in (px.Metric.L2, px.Metric.InnerProduct):
+        ref = px.FlatIndex(dim, metric)
+        ref.add(base)
+        ref.set_search_path("exact")
+        for call, nq in enumerate((37, 5)):
+            q = rng.standard_normal((nq, dim)).astype(np.float32)
+            want_ids, want_d = ref.search_batch(q, k=k)
+            d_q = torch.from_numpy(q).to(dev)
+            out_ids = torch.empty((nq, k), dtype=torch.int64, device=dev)
+            out_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
+            stream = torch.cuda.current_stream(dev)
+            torch.cuda.synchronize()
+            free_before = torch.cuda.mem_get_info(dev)[0]
+            st = lib.px_flat_search_noalloc(
+                ctypes.c_void_p(d_base.data_ptr()), n, dim, int(metric),
+                ctypes.c_void_p(d_q.data_ptr()), nq, k, ctypes.c_void_p(out_ids.data_ptr()),
+                ctypes.c_void_p(out_d.data_ptr()), ctypes.c_void_p(stream.cuda_stream))
+            assert st == 0, px._lib.last_error()
+            torch.cuda.synchronize()
+            if not first:
+                assert torch.cuda.mem_get_info(dev)[0] == free_before, f"call {call} allocated memory"
+            first = False
+            got_ids, got_d = out_ids.cpu().numpy(), out_d.cpu().numpy()
+            assert np.array_equal(got_d.view(np.uint32), want_d.view(np.uint32)), f"call {call}"
+            assert np.array_equal(got_ids, want_ids), f"call {call}"
+
+
+def test_noalloc_rejects_what_does_not_fit(px):
+    lib = px._lib.load()
+    vp = ctypes.c_void_p
+    # dim must be a multiple of 4; nq * k beyond the fixed scratch is refused.
+    assert lib.px_flat_search_noalloc(vp(16), 10, 6, 0, vp(16), 1, 1, vp(16), vp(16), None) == px._lib.PX_EUNSUPPORTED
+    assert "multiple of 4" in px._lib.last_error()
+    assert lib.px_flat_search_noalloc(vp(16), 10, 8, 0, vp(16), 200000, 700, vp(16), vp(16), None) == px._lib.PX_EUNSUPPORTED
+    assert "scratch" in px._lib.last_error()
