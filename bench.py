@@ -180,6 +180,21 @@ def peaks():
                 "source": "fallback"}
 
 
+def ncu_traffic(config, kernel):
+    """Per-launch DRAM bytes of `kernel` on `config` from the committed ncu
+    summary (profiles/traffic.txt), or None if that pair was not captured."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) == 4 and not line.startswith("#") and parts[0] == config and parts[1] == kernel:
+                    return int(parts[2]) + int(parts[3])
+    except OSError:
+        pass
+    return None
+
+
 def cpu_threads():
     import oracle
     return oracle.max_threads()
@@ -354,8 +369,11 @@ def run_ours(args, cfg, rank, world, local_rank):
             flops = 2.0 * nq * n_local * dim
             achieved = flops / avg_s / 1e12
             peak = pk["bf16_tflops_sustained"] / 2.0 / 3.0
+            traffic = ncu_traffic(args.config, "gemm_topk_kernel") if world == 1 else None
             roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                        "frac": achieved / peak, "traffic": None,
+                        "frac": achieved / peak, "traffic": traffic,
+                        "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
+                                        "(profiles/gemm_topk_kernel.md)" if traffic else None,
                         "kernel": "gemm_topk_kernel (tcgen05 kind::tf32, 3 passes)",
                         "kernel_ms": statistics.mean(kernel_ms),
                         "peak_basis": f"3xTF32 rate = bf16_tflops_sustained {pk['bf16_tflops_sustained']} "

@@ -76,8 +76,9 @@ class ShardedFlatIndex:
             self._bufs = {key: dict(
                 ids=torch.empty((nq, k), dtype=torch.int64, device=dev),
                 keys=torch.empty((nq, k), dtype=torch.float32, device=dev),
-                all_ids=torch.empty((self.world, nq, k), dtype=torch.int64, device=dev),
-                all_keys=torch.empty((self.world, nq, k), dtype=torch.float32, device=dev),
+                # rank lists concatenated on dim 0: [world * nq, k] == [world][nq][k]
+                all_ids=torch.empty((self.world * nq, k), dtype=torch.int64, device=dev),
+                all_keys=torch.empty((self.world * nq, k), dtype=torch.float32, device=dev),
                 out_ids=torch.empty((nq, k), dtype=torch.int64, device=dev),
                 out_d=torch.empty((nq, k), dtype=torch.float32, device=dev),
             )}
