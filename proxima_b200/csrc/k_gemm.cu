@@ -36,17 +36,23 @@ namespace px {
 
 namespace {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
-constexpr int BK = 16;  // tf32 per stage row: 64 bytes = one 64B swizzle span
+constexpr int BM = 128;  // queries per query tile (TMEM lanes)
+constexpr int BK = 16;   // tf32 per stage row: 64 bytes = one 64B swizzle span
 constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK * 4;
-constexpr int B_BYTES = BN * BK * 4;
-constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-constexpr int kGemmThreads = 192;
+constexpr int A_BYTES = BM * BK * 4;  // one plane of one query tile per stage
 constexpr uint32_t kTmemCols = 512;
 constexpr int kNumBars = 2 * STAGES + 2 + 2 + 1;  // full, empty, tmem full, tmem empty, done
-constexpr size_t kGemmSmem = 1024 + STAGES * STAGE_BYTES + kNumBars * 8 + 16 + BM * 33 * 4;
+
+// QT query tiles share each base tile of BN(QT) = 256 / QT rows: a stage holds
+// QT x {Qhi, Qlo} and {Xhi, Xlo}, 48 KB for QT = 1 and 2 alike, and the TMEM
+// holds 2 buffers x QT accumulators x BN columns = 512 columns.
+template <int QT> struct Tile {
+  static constexpr int BN = 256 / QT;
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int STAGE_BYTES = QT * 2 * A_BYTES + 2 * B_BYTES;
+  static constexpr int THREADS = 64 + 128 * QT;  // TMA warp, MMA warp, QT epilogue warpgroups
+  static constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + kNumBars * 8 + 16 + 128 * QT * 33 * 4;
+};
 
 __device__ __forceinline__ bool mbar_wait_quiet(uint32_t bar, uint32_t parity) {
   int dummy = 0;
@@ -90,18 +96,22 @@ __device__ __forceinline__ void list_sort(uint64_t (&L)[CAP]) {
   }
 }
 
-template <int CAP, bool L2>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+template <int CAP, bool L2, int QT>
+__global__ void __launch_bounds__(Tile<QT>::THREADS, 1)
 gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
                  const __grid_constant__ CUtensorMap tm_xhi, const __grid_constant__ CUtensorMap tm_xlo,
                  const GemmTopkArgs p) {
+  constexpr int BN = Tile<QT>::BN;
+  constexpr int B_BYTES = Tile<QT>::B_BYTES;
+  constexpr int STAGE_BYTES = Tile<QT>::STAGE_BYTES;
+  constexpr int B_OFF = QT * 2 * A_BYTES;  // {Xhi, Xlo} after the QT query tiles
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
-  float* s_keys = reinterpret_cast<float*>(s_tmem + 4);  // 128 x 33 epilogue key slots
+  float* s_keys = reinterpret_cast<float*>(s_tmem + 4);  // (128 * QT) x 33 epilogue key slots
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -122,7 +132,7 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
     }
     for (int a = 0; a < 2; ++a) {
       tc::mbar_init(tfull_bar(a), 1);
-      tc::mbar_init(tempty_bar(a), 4);
+      tc::mbar_init(tempty_bar(a), 4 * QT);
     }
     tc::mbar_init(done_bar, 1);
     *s_abort = 0;
@@ -157,10 +167,10 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
         issued[s] = false;
         issued_phase[s] = 0;
       }
-      const uint32_t bytes = A_BYTES + B_BYTES + (q_lo ? A_BYTES : 0) + (x_lo ? B_BYTES : 0);
+      const uint32_t bytes = QT * A_BYTES * (q_lo ? 2 : 1) + B_BYTES * (x_lo ? 2 : 1);
       bool ok = true;
       for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
-        const int qt = item % p.T;
+        const int qp = item % p.T;  // group of QT query tiles
         const int split = item / p.T;
         const int t0 = split * p.tiles_per_split;
         const int t1 = min(p.nb, t0 + p.tiles_per_split);
@@ -172,11 +182,14 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
             }
             const uint32_t sbase = smem_base + stage * STAGE_BYTES;
             tc::mbar_arrive_expect_tx(full_bar(stage), bytes);
-            tc::tma_load_2d(sbase, &tm_qhi, full_bar(stage), kc * BK, qt * BM);
-            if (q_lo) tc::tma_load_2d(sbase + A_BYTES, &tm_qlo, full_bar(stage), kc * BK, qt * BM);
-            tc::tma_load_2d(sbase + 2 * A_BYTES, &tm_xhi, full_bar(stage), kc * BK, t * BN);
-            if (x_lo)
-              tc::tma_load_2d(sbase + 2 * A_BYTES + B_BYTES, &tm_xlo, full_bar(stage), kc * BK, t * BN);
+#pragma unroll
+            for (int q = 0; q < QT; ++q) {
+              const int qrow = (qp * QT + q) * BM;
+              tc::tma_load_2d(sbase + q * 2 * A_BYTES, &tm_qhi, full_bar(stage), kc * BK, qrow);
+              if (q_lo) tc::tma_load_2d(sbase + q * 2 * A_BYTES + A_BYTES, &tm_qlo, full_bar(stage), kc * BK, qrow);
+            }
+            tc::tma_load_2d(sbase + B_OFF, &tm_xhi, full_bar(stage), kc * BK, t * BN);
+            if (x_lo) tc::tma_load_2d(sbase + B_OFF + B_BYTES, &tm_xlo, full_bar(stage), kc * BK, t * BN);
             issued[stage] = true;
             issued_phase[stage] = phase;
             if (++stage == STAGES) {
@@ -210,7 +223,6 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
             break;
           }
           tc::tc_fence_after();
-          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
           for (int kc = 0; kc < KC; ++kc) {
             if (!tc::mbar_wait(full_bar(stage), phase, s_abort)) {
               ok = false;
@@ -218,17 +230,21 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
             }
             tc::tc_fence_after();
             const uint32_t sbase = smem_base + stage * STAGE_BYTES;
-            const uint64_t a_hi = tc::sw64_kmajor_desc(sbase);
-            const uint64_t a_lo = tc::sw64_kmajor_desc(sbase + A_BYTES);
-            const uint64_t b_hi = tc::sw64_kmajor_desc(sbase + 2 * A_BYTES);
-            const uint64_t b_lo = tc::sw64_kmajor_desc(sbase + 2 * A_BYTES + B_BYTES);
+            const uint64_t b_hi = tc::sw64_kmajor_desc(sbase + B_OFF);
+            const uint64_t b_lo = tc::sw64_kmajor_desc(sbase + B_OFF + B_BYTES);
 #pragma unroll
-            for (int kk = 0; kk < BK / 8; ++kk) {
-              const uint64_t off = static_cast<uint64_t>(kk * 32) >> 4;  // 32 bytes per K step
-              const uint32_t accumulate = (kc > 0 || kk > 0) ? 1u : 0u;
-              tc::mma_tf32(d_tmem, a_hi + off, b_hi + off, idesc, accumulate);
-              if (x_lo) tc::mma_tf32(d_tmem, a_hi + off, b_lo + off, idesc, 1u);
-              if (q_lo) tc::mma_tf32(d_tmem, a_lo + off, b_hi + off, idesc, 1u);
+            for (int q = 0; q < QT; ++q) {
+              const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((acc * QT + q) * BN);
+              const uint64_t a_hi = tc::sw64_kmajor_desc(sbase + q * 2 * A_BYTES);
+              const uint64_t a_lo = tc::sw64_kmajor_desc(sbase + q * 2 * A_BYTES + A_BYTES);
+#pragma unroll
+              for (int kk = 0; kk < BK / 8; ++kk) {
+                const uint64_t off = static_cast<uint64_t>(kk * 32) >> 4;  // 32 bytes per K step
+                const uint32_t accumulate = (kc > 0 || kk > 0) ? 1u : 0u;
+                tc::mma_tf32(d_tmem, a_hi + off, b_hi + off, idesc, accumulate);
+                if (x_lo) tc::mma_tf32(d_tmem, a_hi + off, b_lo + off, idesc, 1u);
+                if (q_lo) tc::mma_tf32(d_tmem, a_lo + off, b_hi + off, idesc, 1u);
+              }
             }
             tc::mma_commit(empty_bar(stage));
             if (++stage == STAGES) {
@@ -250,14 +266,16 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int wg = (warp - 2) >> 2;  // which query tile of the group
+    const int quarter = warp & 3;    // TMEM lanes this warp may access
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+    float* slot = s_keys + (wg * 128 + row_in_tile) * 33;
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
     for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
-      const int qt = item % p.T;
+      const int qp = item % p.T;
       const int split = item / p.T;
       const int t0 = split * p.tiles_per_split;
       const int t1 = min(p.nb, t0 + p.tiles_per_split);
@@ -278,10 +296,11 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
         const int64_t row0 = static_cast<int64_t>(t) * BN;
         // Columns of this tile that are real rows (the last tile may be short).
         const int valid_cols = p.n - row0 < BN ? static_cast<int>(p.n - row0) : BN;
+        const uint32_t col0 = static_cast<uint32_t>((acc * QT + wg) * BN);
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t v[32];
-          tc::tmem_ld_32x32b_x32(lane_addr + static_cast<uint32_t>(acc * BN + c * 32), v);
+          tc::tmem_ld_32x32b_x32(lane_addr + col0 + static_cast<uint32_t>(c * 32), v);
           tc::tmem_ld_wait();
           const int64_t rbase = row0 + c * 32;
           const int nvalid = valid_cols - c * 32;
@@ -309,7 +328,6 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
           if (pass) {
             // Rare path, one copy of the insertion code: keys go through
             // this thread's shared-memory slot so they can be indexed.
-            float* slot = s_keys + row_in_tile * 33;
 #pragma unroll
             for (int j = 0; j < 32; ++j) slot[j] = key[j];
             while (pass) {
@@ -336,7 +354,7 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
       }
       if (!ok) break;
       list_sort<CAP>(L);
-      const int64_t qidx = static_cast<int64_t>(qt) * BM + row_in_tile;
+      const int64_t qidx = static_cast<int64_t>(qp * QT + wg) * BM + row_in_tile;
       if (qidx < p.nq) {
         uint64_t* out = p.partial + (qidx * p.S + split) * CAP;
 #pragma unroll
@@ -365,13 +383,13 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-template <int CAP, bool L2>
+template <int CAP, bool L2, int QT>
 cudaError_t launch_typed(const GemmTopkArgs& a, const CUtensorMap* maps, int grid, cudaStream_t stream) {
-  auto kern = gemm_topk_kernel<CAP, L2>;
+  auto kern = gemm_topk_kernel<CAP, L2, QT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(kGemmSmem));
+                                       static_cast<int>(Tile<QT>::SMEM));
   if (e != cudaSuccess) return e;
-  kern<<<grid, kGemmThreads, kGemmSmem, stream>>>(maps[0], maps[1], maps[2], maps[3], a);
+  kern<<<grid, Tile<QT>::THREADS, Tile<QT>::SMEM, stream>>>(maps[0], maps[1], maps[2], maps[3], a);
   return cudaGetLastError();
 }
 
@@ -399,23 +417,26 @@ int gemm_cap_for(int k) {
   return 0;
 }
 
-size_t gemm_smem_bytes() { return kGemmSmem; }
+int gemm_qt_for(int k) { return gemm_cap_for(k) == 32 ? 2 : 1; }
+
+int gemm_bn_for(int k) { return 256 / gemm_qt_for(k); }
 
 cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const float* q_hi, const float* q_lo,
                              int64_t q_rows, const float* x_hi, const float* x_lo, int grid,
                              cudaStream_t stream) {
   if (a.ld % BK != 0) return cudaErrorInvalidValue;
+  const int qt = gemm_qt_for(a.k);
   CUtensorMap maps[4];
   cudaError_t e = encode_plane_map(&maps[0], q_hi, q_rows, a.ld, BM);
   if (e == cudaSuccess) e = encode_plane_map(&maps[1], q_lo, q_rows, a.ld, BM);
-  if (e == cudaSuccess) e = encode_plane_map(&maps[2], x_hi, a.n, a.ld, BN);
-  if (e == cudaSuccess) e = encode_plane_map(&maps[3], x_lo, a.n, a.ld, BN);
+  if (e == cudaSuccess) e = encode_plane_map(&maps[2], x_hi, a.n, a.ld, 256 / qt);
+  if (e == cudaSuccess) e = encode_plane_map(&maps[3], x_lo, a.n, a.ld, 256 / qt);
   if (e != cudaSuccess) return e;
   const int cap = gemm_cap_for(a.k);
-  if (cap == 32) return a.l2 ? launch_typed<32, true>(a, maps, grid, stream)
-                             : launch_typed<32, false>(a, maps, grid, stream);
-  if (cap == 64) return a.l2 ? launch_typed<64, true>(a, maps, grid, stream)
-                             : launch_typed<64, false>(a, maps, grid, stream);
+  if (cap == 32) return a.l2 ? launch_typed<32, true, 2>(a, maps, grid, stream)
+                             : launch_typed<32, false, 2>(a, maps, grid, stream);
+  if (cap == 64) return a.l2 ? launch_typed<64, true, 1>(a, maps, grid, stream)
+                             : launch_typed<64, false, 1>(a, maps, grid, stream);
   return cudaErrorInvalidValue;
 }
 

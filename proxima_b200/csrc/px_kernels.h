@@ -104,9 +104,9 @@ struct GemmTopkArgs {
   int64_t n;            // shard rows
   int ld;               // row stride (floats), multiple of 16
   int k;
-  int T;                // query tiles of 128
+  int T;                // groups of gemm_qt_for(k) query tiles of 128
   int S;                // base splits
-  int tiles_per_split;  // base tiles of 256 rows per split
+  int tiles_per_split;  // base tiles of gemm_bn_for(k) rows per split
   int nb;               // base tiles
   int n_items;          // T * S
   bool l2;
@@ -117,7 +117,8 @@ struct GemmTopkArgs {
   int* err;             // device word raised on a timed-out wait
 };
 int gemm_cap_for(int k);  // candidates kept per query (0: k unsupported)
-size_t gemm_smem_bytes();
+int gemm_qt_for(int k);   // query tiles of 128 per CTA (2 for k <= 16, else 1)
+int gemm_bn_for(int k);   // base rows per tile (256 / qt)
 cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const float* q_hi, const float* q_lo,
                              int64_t q_rows, const float* x_hi, const float* x_lo, int grid,
                              cudaStream_t stream);

@@ -51,8 +51,11 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
   if (gemm) {
     plan.path = FlatPath::Gemm;
     plan.cap = cap;
-    const int64_t T = (nq + 127) / 128;
-    const int64_t nb = std::max<int64_t>(1, (sh.n + 255) / 256);
+    // Work items: (group of QT query tiles, run of base tiles of BN rows).
+    const int qt = gemm_qt_for(k);
+    const int bn = gemm_bn_for(k);
+    const int64_t T = ((nq + 127) / 128 + qt - 1) / qt;
+    const int64_t nb = std::max<int64_t>(1, (sh.n + bn - 1) / bn);
     // Splits so that T * S is a whole number of waves of one CTA per SM.
     int64_t S = sh.sms / gcd64(T, sh.sms);
     while (S * 2 <= 1024 && S * T < 2 * sh.sms && S * 2 <= nb) S *= 2;
@@ -66,7 +69,7 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
     plan.tiles_per_split = static_cast<int>(tps);
     plan.n_items = static_cast<int>(T * S);
     plan.grid = static_cast<int>(std::min<int64_t>(sh.sms, T * S));
-    plan.q_rows = T * 128;
+    plan.q_rows = T * qt * 128;
     c.take(sizeof(float) * static_cast<size_t>(plan.q_rows) * h->ld);  // q hi
     c.take(sizeof(float) * static_cast<size_t>(plan.q_rows) * h->ld);  // q lo
     c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * S * cap);      // split lists
