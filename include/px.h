@@ -105,7 +105,7 @@ PX_API int32_t px_flat_metric(const px_flat* h);
 /* Kernel path for flat searches: AUTO picks the exact streaming scan for
  * small batches (and masks) and the tensor-core path otherwise; EXACT and
  * TENSOR force one (TENSOR fails with PX_EUNSUPPORTED where it cannot serve
- * the request, e.g. k > 40 or a mask). Results are identical on every path. */
+ * the request, e.g. k > 224 or a mask). Results are identical on every path. */
 enum { PX_PATH_AUTO = 0, PX_PATH_EXACT = 1, PX_PATH_TENSOR = 2 };
 PX_API px_status px_flat_set_path(px_flat* h, int32_t mode);
 

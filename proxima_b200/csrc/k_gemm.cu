@@ -413,7 +413,14 @@ cudaError_t encode_plane_map(CUtensorMap* map, const float* plane, int64_t rows,
 
 int gemm_cap_for(int k) {
   if (k <= 16) return 32;
+  if (k <= 224) return 64;
+  return 0;
+}
+
+int gemm_cands_for(int k) {
+  if (k <= 16) return 32;
   if (k <= 40) return 64;
+  if (k <= 224) return (k + 32 + 31) / 32 * 32;
   return 0;
 }
 

@@ -24,6 +24,7 @@ namespace px {
 namespace {
 
 constexpr int kRescoreWarps = 4;
+constexpr int kMaxCands = 256;
 
 template <bool L2>
 __global__ void __launch_bounds__(kRescoreWarps * 32)
@@ -33,8 +34,8 @@ rescore_kernel(const RescoreArgs a) {
   const int dq = (a.d + 3) & ~3;
   float* s_q = reinterpret_cast<float*>(smem_raw) + warp * dq;
   uint64_t* s_c = reinterpret_cast<uint64_t*>(reinterpret_cast<float*>(smem_raw) + kRescoreWarps * dq) +
-                  warp * 2 * 64;
-  uint64_t* s_sorted = s_c + 64;
+                  warp * 2 * kMaxCands;
+  uint64_t* s_sorted = s_c + kMaxCands;
   const int64_t q = static_cast<int64_t>(blockIdx.x) * kRescoreWarps + warp;
   if (q >= a.nq) return;
 
@@ -73,9 +74,25 @@ rescore_kernel(const RescoreArgs a) {
   }
   __syncwarp();
 
-  // Certificate.
+  // Certificate. Every row outside the candidate set has an approximate key
+  // >= min(A_cap, max of every full split list): when the per-split lists
+  // are shorter than the merged set, a split can hide rows below A_cap.
   int ok = 1;
-  const uint64_t last = mq[a.cap - 1];
+  uint64_t last = mq[a.cap - 1];
+  if (a.list_cap < a.cap) {
+    uint64_t m = PX_EMPTY;
+    const uint64_t* ql = a.lists + q * static_cast<int64_t>(a.nlists) * a.list_cap;
+    for (int j = lane; j < a.nlists; j += 32) {
+      const uint64_t lmax = ql[static_cast<int64_t>(j) * a.list_cap + a.list_cap - 1];
+      m = lmax < m ? lmax : m;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const uint64_t o = __shfl_xor_sync(0xffffffffu, m, off);
+      m = o < m ? o : m;
+    }
+    last = m < last ? m : last;
+  }
   const uint64_t kth = s_sorted[a.k - 1];
   if (last != PX_EMPTY && kth != PX_EMPTY) {
     const double qn = sqrt(qsq);
@@ -131,9 +148,9 @@ __global__ void scatter_cands_kernel(const uint64_t* __restrict__ src, int k, co
 
 cudaError_t launch_rescore(const RescoreArgs& a, cudaStream_t stream) {
   if (a.nq == 0) return cudaSuccess;
-  if (a.cap > 64 || a.k > a.cap) return cudaErrorInvalidValue;
+  if (a.cap > kMaxCands || a.k > a.cap) return cudaErrorInvalidValue;
   const int dq = (a.d + 3) & ~3;
-  const size_t smem = sizeof(float) * kRescoreWarps * dq + sizeof(uint64_t) * kRescoreWarps * 128;
+  const size_t smem = sizeof(float) * kRescoreWarps * dq + sizeof(uint64_t) * kRescoreWarps * 2 * kMaxCands;
   const unsigned blocks = static_cast<unsigned>((a.nq + kRescoreWarps - 1) / kRescoreWarps);
   if (a.l2) {
     cudaError_t e = cudaFuncSetAttribute(rescore_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,

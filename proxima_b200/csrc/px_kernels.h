@@ -116,7 +116,8 @@ struct GemmTopkArgs {
   uint64_t* partial;    // [nq][S][cap] sorted approximate candidates
   int* err;             // device word raised on a timed-out wait
 };
-int gemm_cap_for(int k);  // candidates kept per query (0: k unsupported)
+int gemm_cap_for(int k);    // candidates kept per (query, split) in registers (0: unsupported)
+int gemm_cands_for(int k);  // candidates per query after the split merge (<= 256)
 int gemm_qt_for(int k);   // query tiles of 128 per CTA (2 for k <= 16, else 1)
 int gemm_bn_for(int k);   // base rows per tile (256 / qt)
 cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const float* q_hi, const float* q_lo,
@@ -127,8 +128,11 @@ cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const float* q_hi, const flo
 struct RescoreArgs {
   const uint64_t* merged;  // [nq][cap] sorted approximate candidates
   int64_t nq;
-  int cap;
+  int cap;                 // candidates per query (<= 256)
   int k;
+  const uint64_t* lists;   // [nq][nlists][list_cap] per-split lists (for the bound)
+  int nlists;
+  int list_cap;
   const float* queries;    // nq x d
   const float* base;       // shard fp32 rows, stride ld
   int ld;

@@ -51,6 +51,7 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
   if (gemm) {
     plan.path = FlatPath::Gemm;
     plan.cap = cap;
+    plan.cands = gemm_cands_for(k);
     // Work items: (group of QT query tiles, run of base tiles of BN rows).
     const int qt = gemm_qt_for(k);
     const int bn = gemm_bn_for(k);
@@ -73,7 +74,7 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
     c.take(sizeof(float) * static_cast<size_t>(plan.q_rows) * h->ld);  // q hi
     c.take(sizeof(float) * static_cast<size_t>(plan.q_rows) * h->ld);  // q lo
     c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * S * cap);      // split lists
-    c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * cap);          // merged
+    c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.cands);   // merged
     c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * k);            // final
     c.take(sizeof(int) * static_cast<size_t>(nq));                     // status
     c.take(sizeof(int) * static_cast<size_t>(nq));                     // fail list
@@ -152,7 +153,8 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   float* q_hi = static_cast<float*>(c.take(qplane));
   float* q_lo = static_cast<float*>(c.take(qplane));
   uint64_t* partial = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.S * cap));
-  uint64_t* merged = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * cap));
+  const int cands = plan.cands;
+  uint64_t* merged = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * cands));
   plan.final_cands = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * k));
   int* status = static_cast<int*>(c.take(sizeof(int) * static_cast<size_t>(nq)));
   int* fail_list = static_cast<int*>(c.take(sizeof(int) * static_cast<size_t>(nq)));
@@ -183,13 +185,16 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   e = launch_gemm_topk(g, q_hi, q_lo, plan.q_rows, sh.hi, sh.lo, plan.grid, stream);
   if (prof) cudaEventRecord(sh.ev_stop, stream);
   if (e != cudaSuccess) return cuda_status(e, "tensor-core kernel launch");
-  e = launch_merge_lists(partial, nq, plan.S, cap, cap, merged, stream);
+  e = launch_merge_lists(partial, nq, plan.S, cap, cands, merged, stream);
   if (e != cudaSuccess) return cuda_status(e, "split merge launch");
   RescoreArgs r;
   r.merged = merged;
   r.nq = nq;
-  r.cap = cap;
+  r.cap = cands;
   r.k = k;
+  r.lists = partial;
+  r.nlists = plan.S;
+  r.list_cap = cap;
   r.queries = d_q;
   r.base = sh.x;
   r.ld = h->ld;

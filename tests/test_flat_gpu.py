@@ -274,6 +274,7 @@ def _run_path(pxm, data, metric, queries, k, path):
 @pytest.mark.parametrize("n,dim,nq,k", [
     (5000, 32, 16, 10), (20000, 64, 128, 10), (9000, 128, 300, 16), (12345, 24, 77, 1),
     (30000, 96, 200, 40), (8192, 768, 130, 10), (4096, 384, 129, 5),
+    (20000, 64, 140, 100), (9000, 48, 33, 224), (12000, 128, 260, 41),
 ])
 def test_tensor_path_parity(pxm, metric, n, dim, nq, k):
     data = _data.unit_gaussian(n, dim, n + dim) if metric == O.IP else \
@@ -323,4 +324,6 @@ def test_tensor_path_rejects_what_it_cannot_serve(pxm):
     idx.add(O.gen_uniform(5000, 16, 1))
     idx.set_search_path("tensor")
     with pytest.raises(pxm.PxError):
-        idx.search_batch(O.gen_uniform(32, 16, 2), k=41)
+        idx.search_batch(O.gen_uniform(32, 16, 2), k=225)
+    with pytest.raises(pxm.PxError):
+        idx.search_batch_filtered(O.gen_uniform(32, 16, 2), np.ones(5000, bool), k=10)
