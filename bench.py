@@ -52,6 +52,8 @@ CONFIGS = {
     "c5": ("l2", 100_000_000, 96, 10_000, 10, "mixture"),
     # profiling case for ncu: config 4's distribution at 1/40 of the rows
     "prof": ("ip", 262_144, 768, 1_024, 10, "unit"),
+    # PQ ADC scan (config 3): m=16 x 256 centroids trained on a 100k sample
+    "c3": ("pq-l2", 1_000_000, 128, 1_000, 10, "sift"),
 }
 WORKLOAD_TEXT = {
     "c4k10": "exact IP kNN, base 10,000,000x768 unit-norm N(0,1), 10,000 queries, k=10 (config 4 at k=10)",
@@ -62,6 +64,8 @@ WORKLOAD_TEXT = {
     "c2q1": "exact L2 kNN, base 1,000,000x128 SIFT-like, 1 query, k=10 (config 2)",
     "c5": "exact L2 kNN, base 100,000,000x96 Gaussian mixture, one 10,000-query batch, k=10 (config 5)",
     "prof": "profiling case: exact IP kNN, base 262,144x768 unit-norm N(0,1), 1,024 queries, k=10",
+    "c3": "PQ ADC scan, L2, m=16 x 256 centroids (k-means on a 100,000-row sample), 1,000,000 codes, "
+          "1,000 queries, k=10 (config 3)",
 }
 BLOCK = 1 << 18  # rows generated per seeded block
 
@@ -256,6 +260,89 @@ def run_reference(args, cfg, rank, world):
                                    "C++ restatement of FlatIndex::search_batch (flat.rs:150-191), "
                                    "all host threads (the Rust crate cannot be built here)"},
         "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_pq(args, cfg, rank, world, local_rank):
+    """Config 3: the PQ ADC scan through PqIndex (host buffers, one GPU)."""
+    import torch
+    import proxima_b200 as px
+    from proxima_b200 import _lib
+
+    metric, n, dim, nq, k, kind = cfg
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"metric": f"PQ ADC QPS (k={k})", "unavailable": "PQ bench runs on one GPU"}))
+        return 0
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(local_rank)
+    base = host_copy(kind, n, dim, args.seed, device)
+    queries = gen_queries(kind, nq, dim, args.seed, device).cpu().numpy()
+    t0 = time.time()
+    pq = px.PqIndex(dim, px.Metric.L2, m=16, nbits=8, train_iters=25, train_sample=100_000, seed=args.seed,
+                    devices=[local_rank])
+    pq.train(base)
+    pq.add(base)
+    build_s = time.time() - t0
+    for _ in range(args.warmup):
+        pq.search_batch(queries, k=k)
+    _lib.set_profiling(True)
+    launches0 = _lib.launch_count()
+    kernel_ms, times = [], []
+    with ClockSampler(local_rank) as clocks:
+        for _ in range(args.steps):
+            t = time.perf_counter()
+            ids, d = pq.search_batch(queries, k=k)
+            times.append(time.perf_counter() - t)
+            kernel_ms.append(pq.last_search_profile()["main_kernel_ms"])
+    _lib.set_profiling(False)
+    launches = _lib.launch_count() - launches0
+    step_s = statistics.mean(times)
+    kern_s = statistics.mean(kernel_ms) / 1e3
+    m = 16
+    gathers = float(nq) * n * m
+    byts = n * m + nq * (dim * 4 + m * 256 * 4)
+    pk = peaks()
+    clock = clocks.summary()
+    sm_ghz = (clock.get("sm_mhz") or 1965.0) / 1e3
+    smem_peak = 148 * 32 * sm_ghz  # conflict-free 32-bit gathers per ns
+    cpu = parity = None
+    if not args.no_cpu_baseline:
+        import oracle as O
+        from tests import _parity
+        books = pq.codebooks
+        codes = pq.encode(base)
+        sample = min(args.cpu_sample * 4, nq)
+        t = time.perf_counter()
+        ref_ids, ref_d = O.pq_search_batch(books, O.L2, codes, queries[:sample], k, num_threads=0)
+        dt = time.perf_counter() - t
+        cpu = {"value": sample / dt, "unit": "queries/s", "cores": cpu_threads(), "kind": "port",
+               "sample": f"first {sample} of the {nq} queries against all {n} codes ({dt:.2f} s); "
+                         "C++ restatement of PqIndex::search_batch, all host threads"}
+        try:
+            ties = _parity.check(ids[:sample], d[:sample], ref_ids, ref_d,
+                                 _parity.pq_natural(books, O.L2, codes, queries[:sample]))
+            parity = {"queries": sample, "ok": True, "tie_positions": int(ties)}
+        except AssertionError as e:
+            parity = {"queries": sample, "ok": False, "error": str(e)[:200]}
+    line = {
+        "metric": f"PQ ADC QPS (k={k})", "value": nq / step_s, "unit": "queries/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * step_s, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32 (u8 codes)", "data": "synthetic",
+        "config": {"workload": WORKLOAD_TEXT[args.config], "n_codes": n, "dim": dim, "m": m, "nq": nq, "k": k,
+                   "build_s": round(build_s, 2), "timing": "host-to-host PqIndex.search_batch"},
+        "roofline": {"bound": "hbm", "achieved": byts / kern_s / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": byts / kern_s / 1e9 / pk["hbm_gbs"], "traffic": None, "kernel": "pq_scan_kernel",
+                     "kernel_ms": 1e3 * kern_s, "algorithmic_bytes_per_launch": byts,
+                     "smem_gathers": {"achieved_per_ns": gathers / kern_s / 1e9, "peak_per_ns": smem_peak,
+                                      "frac": gathers / kern_s / 1e9 / smem_peak,
+                                      "basis": "nq*n*m LUT gathers vs 148 SMs x 32 conflict-free lanes x SM clock"}},
+        "cpu_baseline": cpu, "parity_sample": parity,
+        "e2e": {"value": nq / step_s, "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
+                "d2h_bytes_per_step": int(nq * k * 12)},
+        "clocks": clock, "gpu_launches": int(launches),
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -460,6 +547,8 @@ def main(argv=None):
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if cfg[0].startswith("pq"):
+            return run_pq(args, cfg, rank, world, local_rank)
         return run_ours(args, cfg, rank, world, local_rank)
     finally:
         if world > 1 and dist.is_initialized():

@@ -113,7 +113,7 @@ PX_API px_status px_flat_set_path(px_flat* h, int32_t mode);
  * dominant kernel of each search is bracketed by CUDA events on the
  * launching stream; px_flat_last_profile waits for them and reports. */
 typedef struct px_search_profile {
-  int32_t path;             /* 0 exact scan, 1 tensor-core path */
+  int32_t path;             /* 0 exact scan, 1 tensor-core path, 2 PQ ADC scan */
   int32_t launches;         /* kernels the search launched on the first shard */
   int32_t fallback_queries; /* queries re-run by the exact scan (certificate) */
   int32_t profiled;         /* 1 if main_kernel_ms is valid */
@@ -198,6 +198,8 @@ PX_API px_status px_pq_add_codes(px_pq* h, const uint8_t* codes, int64_t n);
 /* ProductQuantizer::encode_into (pq.rs:107-121) for n vectors -> n x m codes. */
 PX_API px_status px_pq_encode(const px_pq* h, const float* vectors, int64_t n, uint8_t* out_codes);
 PX_API int64_t px_pq_size(const px_pq* h);
+/* As px_flat_last_profile, for the last PQ search (path = 2, the ADC scan). */
+PX_API px_status px_pq_last_profile(const px_pq* h, px_search_profile* out);
 
 /* PqIndex::search_batch (pq.rs:349-396) and its filtered form. */
 PX_API px_status px_pq_search(const px_pq* h, const float* queries, int64_t nq, int32_t k,

@@ -412,6 +412,15 @@ class PqIndex:
     def metric(self) -> Metric:
         return self._metric
 
+    def last_search_profile(self) -> dict:
+        """Kernel launches and (with profiling on) the ADC scan's device time
+        of the last search."""
+        self._trained("index is not trained")
+        prof = _lib.SearchProfile()
+        _lib.check(self._lib.px_pq_last_profile(self._h, ctypes.byref(prof)))
+        return {"path": "pq", "launches": prof.launches,
+                "main_kernel_ms": prof.main_kernel_ms if prof.profiled else None}
+
     @property
     def codebooks(self) -> np.ndarray:
         """The trained codebooks, shape (m, 2**nbits, dim // m)."""

@@ -80,6 +80,7 @@ SIGNATURES = {
     "px_pq_add_codes": (_i32, [_vp, _u8p, _i64]),
     "px_pq_encode": (_i32, [_vp, _f32p, _i64, _u8p]),
     "px_pq_size": (_i64, [_vp]),
+    "px_pq_last_profile": (_i32, [_vp, _vp]),
     "px_pq_search": (_i32, [_vp, _f32p, _i64, _i32, _i64p, _f32p]),
     "px_pq_search_filtered": (_i32, [_vp, _f32p, _i64, _i32, _u8p, _i64p, _f32p]),
 }

@@ -17,8 +17,15 @@ namespace px {
 
 namespace {
 
-constexpr int kPqThreads = 256;
-constexpr int kPqRowsPerIter = 256;
+constexpr int kPqThreads = 512;       // 16 warps: enough to hide the LUT-gather latency
+constexpr int kPqRowsPerIter = 512;   // kSlots (threads / G) x G rows per thread
+
+// 32-bit shared-memory load (the LUT gathers are the kernel's hot loop).
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
 
 __global__ void pq_lut_kernel(const float* __restrict__ books, int m, int ksub, int dsub, bool l2,
                               const float* __restrict__ queries, float* __restrict__ lut) {
@@ -62,43 +69,63 @@ pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
   __syncthreads();
 
   const int g = tid % G;
-  const int slot = tid / G;               // 0 .. 256/G - 1
+  const int slot = tid / G;               // 0 .. kPqThreads/G - 1
   constexpr int kSlots = kPqThreads / G;  // codes per step
   const int64_t row_begin = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
   const int64_t row_end = min(n, row_begin + rows_per_cta);
   const bool vec16 = (m & 15) == 0;
+  const uint32_t lut_addr = static_cast<uint32_t>(__cvta_generic_to_shared(s_lut));
   uint64_t thr = PX_EMPTY;
 
   for (int64_t it = row_begin; it < row_end; it += kPqRowsPerIter) {
-#pragma unroll 1
-    for (int step = 0; step < G; ++step) {
-      const int64_t r = it + step * kSlots + slot;
-      if (r < row_end && g < gcount && (mask == nullptr || mask[r] != 0)) {
-        const uint8_t* code = codes + r * m;
-        float key = 0.0f;
-        if (vec16) {
-          for (int b = 0; b < m; b += 16) {
-            const uint4 w = __ldg(reinterpret_cast<const uint4*>(code + b));
-            const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+    // Each thread scores G rows per iteration for its query g. The G rows'
+    // codes are loaded first and their m-long addition chains interleaved
+    // (G independent chains per thread); every chain keeps the reference's
+    // sub order, so the keys stay bit-exact.
+    bool ok[G];
+    int64_t rr[G];
 #pragma unroll
-            for (int wi = 0; wi < 4; ++wi) {
+    for (int i = 0; i < G; ++i) {
+      rr[i] = it + i * kSlots + slot;
+      ok[i] = rr[i] < row_end && g < gcount && (mask == nullptr || mask[rr[i]] != 0);
+    }
+    float key[G];
 #pragma unroll
-              for (int bi = 0; bi < 4; ++bi) {
-                const int sub = b + wi * 4 + bi;
-                const uint32_t c = (words[wi] >> (8 * bi)) & 0xFFu;
-                key = __fadd_rn(key, s_lut[(sub * ksub + c) * G + g]);
-              }
+    for (int i = 0; i < G; ++i) key[i] = 0.0f;
+    if (vec16) {
+      for (int b = 0; b < m; b += 16) {
+        uint4 w[G];
+#pragma unroll
+        for (int i = 0; i < G; ++i)
+          w[i] = ok[i] ? __ldg(reinterpret_cast<const uint4*>(codes + rr[i] * m + b)) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+#pragma unroll
+          for (int bi = 0; bi < 4; ++bi) {
+            const int sub = b + wi * 4 + bi;
+            const uint32_t lsub = lut_addr + static_cast<uint32_t>((sub * ksub * G + g) * 4);
+#pragma unroll
+            for (int i = 0; i < G; ++i) {
+              const uint32_t word = wi == 0 ? w[i].x : (wi == 1 ? w[i].y : (wi == 2 ? w[i].z : w[i].w));
+              const uint32_t c = (word >> (8 * bi)) & 0xFFu;
+              key[i] = __fadd_rn(key[i], lds_f32(lsub + c * (G * 4)));
             }
           }
-        } else {
-          for (int sub = 0; sub < m; ++sub) {
-            const uint32_t c = code[sub];
-            key = __fadd_rn(key, s_lut[(sub * ksub + c) * G + g]);
-          }
         }
-        topk.offer(g, pack_cand(key, static_cast<uint32_t>(r)), thr);
+      }
+    } else {
+      for (int sub = 0; sub < m; ++sub) {
+        const uint32_t lsub = lut_addr + static_cast<uint32_t>((sub * ksub * G + g) * 4);
+#pragma unroll
+        for (int i = 0; i < G; ++i) {
+          const uint32_t c = ok[i] ? codes[rr[i] * m + sub] : 0u;
+          key[i] = __fadd_rn(key[i], lds_f32(lsub + c * (G * 4)));
+        }
       }
     }
+#pragma unroll
+    for (int i = 0; i < G; ++i)
+      if (ok[i]) topk.offer(g, pack_cand(key[i], static_cast<uint32_t>(rr[i])), thr);
     __syncthreads();
     topk.maybe_compact(k, kPqRowsPerIter, tid, kPqThreads);
     thr = s_thr[g];
@@ -136,8 +163,8 @@ cudaError_t launch_pq_buf(const PqScanArgs& a, cudaStream_t stream) {
 }
 
 int pq_buf_for(int k) {
-  if (k + kPqRowsPerIter <= 512) return 512;
-  return 1024;
+  if (k + kPqRowsPerIter <= 1024) return 1024;
+  return 2048;
 }
 
 // Nearest centroid: grid.y = subspace, one thread per vector. All threads of
@@ -166,7 +193,7 @@ __global__ void nearest_centroid_kernel(const float* __restrict__ vectors, int64
 
 }  // namespace
 
-int pq_max_k() { return 1024 - kPqRowsPerIter; }
+int pq_max_k() { return 2048 - kPqRowsPerIter; }
 
 size_t pq_smem_for(int group, int m, int ksub, int k) {
   const int buf = pq_buf_for(k);
@@ -174,10 +201,10 @@ size_t pq_smem_for(int group, int m, int ksub, int k) {
          sizeof(float) * static_cast<size_t>(group) * m * ksub;
 }
 
-int pq_group_for(int m, int ksub, int64_t nq) {
-  const size_t lut_budget = 160 * 1024;
+int pq_group_for(int m, int ksub, int64_t nq, int k) {
+  const size_t budget = 200 * 1024;
   int g = 8;
-  while (g > 1 && (static_cast<size_t>(g) * m * ksub * sizeof(float) > lut_budget || g / 2 >= nq)) g >>= 1;
+  while (g > 1 && (pq_smem_for(g, m, ksub, k) > budget || g / 2 >= nq)) g >>= 1;
   return g;
 }
 
@@ -189,8 +216,8 @@ cudaError_t launch_pq_lut(const float* books, int m, int ksub, int dsub, bool l2
 }
 
 cudaError_t launch_pq_scan(const PqScanArgs& a, cudaStream_t stream) {
-  if (pq_buf_for(a.k) == 512) return launch_pq_buf<512>(a, stream);
-  return launch_pq_buf<1024>(a, stream);
+  if (pq_buf_for(a.k) == 1024) return launch_pq_buf<1024>(a, stream);
+  return launch_pq_buf<2048>(a, stream);
 }
 
 cudaError_t launch_nearest_centroid(const float* vectors, int64_t n, int m, int dsub, int ksub,

@@ -76,7 +76,7 @@ struct PqScanArgs {
   uint64_t* partial;       // [nq][ncta][k]
 };
 cudaError_t launch_pq_scan(const PqScanArgs& a, cudaStream_t stream);
-int pq_group_for(int m, int ksub, int64_t nq);
+int pq_group_for(int m, int ksub, int64_t nq, int k);
 size_t pq_smem_for(int group, int m, int ksub, int k);
 int pq_max_k();
 

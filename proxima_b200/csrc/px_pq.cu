@@ -48,10 +48,16 @@ struct PqShard {
   px::DevBuf stage;
   int64_t* out_ids = nullptr;
   float* out_dists = nullptr;
+  cudaEvent_t ev_start = nullptr, ev_stop = nullptr;  // bracket the scan kernel when profiling
+  bool last_profiled = false;
+  int last_launches = 0;
 
   void release() {
     px::DeviceGuard g(device);
     if (stream) cudaStreamSynchronize(stream);
+    if (ev_start) cudaEventDestroy(ev_start);
+    if (ev_stop) cudaEventDestroy(ev_stop);
+    ev_start = ev_stop = nullptr;
     if (codes) cudaFree(codes);
     if (books) cudaFree(books);
     codes = nullptr;
@@ -147,7 +153,7 @@ static px_status pq_shard_search(const px_pq* h, PqShard& sh, const float* d_q, 
   const bool l2 = h->metric == PX_METRIC_L2;
   px_status s = sh.segs.sync_device();
   if (s != PX_OK) return s;
-  const int group = pq_group_for(h->m, h->ksub, nq);
+  const int group = pq_group_for(h->m, h->ksub, nq, k);
   const int64_t groups = (nq + group - 1) / group;
   if (groups > 65535) return set_error(PX_EUNSUPPORTED, "too many queries in one call");
   const size_t smem = pq_smem_for(group, h->m, h->ksub, k);
@@ -156,10 +162,10 @@ static px_status pq_shard_search(const px_pq* h, PqShard& sh, const float* d_q, 
   const int64_t target = static_cast<int64_t>(sh.sms) * std::min(per_sm, 4) * 2;
   const int64_t n = std::max<int64_t>(sh.n, 1);
   int64_t ncta = std::max<int64_t>(1, (target + groups - 1) / groups);
-  ncta = std::min<int64_t>(ncta, (n + 255) / 256);
+  ncta = std::min<int64_t>(ncta, (n + 511) / 512);
   ncta = std::min<int64_t>(ncta, 1024);
   int64_t rows = (n + ncta - 1) / ncta;
-  rows = (rows + 255) / 256 * 256;
+  rows = (rows + 511) / 512 * 512;
   ncta = (n + rows - 1) / rows;
 
   px::Carver c;
@@ -188,8 +194,14 @@ static px_status pq_shard_search(const px_pq* h, PqShard& sh, const float* d_q, 
   a.rows_per_cta = rows;
   a.mask = d_mask;
   a.partial = partial;
+  const bool prof = px::g_profiling.load() != 0;
+  sh.last_profiled = prof;
+  if (prof) cudaEventRecord(sh.ev_start, stream);
   e = launch_pq_scan(a, stream);
+  if (prof) cudaEventRecord(sh.ev_stop, stream);
   if (e != cudaSuccess) return cuda_status(e, "PQ scan launch");
+  px::g_launches += 4;  // table, scan, merge, emit
+  sh.last_launches = 4;
   e = launch_merge_lists(partial, nq, static_cast<int>(ncta), k, k, cands, stream);
   if (e != cudaSuccess) return cuda_status(e, "merge launch");
   e = launch_emit(cands, nq, k, l2, natural, sh.segs.view(0), d_ids, d_dists, stream);
@@ -409,6 +421,8 @@ PX_API px_status px_pq_create(int32_t dim, int32_t m, int32_t nbits, int32_t met
     const size_t bb = sizeof(float) * h->books.size();
     cudaError_t e = cudaStreamCreateWithFlags(&sh.stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&sh.books, bb);
+    if (e == cudaSuccess) e = cudaEventCreate(&sh.ev_start);
+    if (e == cudaSuccess) e = cudaEventCreate(&sh.ev_stop);
     if (e == cudaSuccess) e = cudaMemcpy(sh.books, h->books.data(), bb, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
       px_status st = cuda_status(e, "PQ create");
@@ -433,6 +447,28 @@ PX_API px_status px_pq_destroy(px_pq* h) {
 }
 
 PX_API int64_t px_pq_size(const px_pq* h) { return h ? h->total : 0; }
+
+PX_API px_status px_pq_last_profile(const px_pq* h, px_search_profile* out) {
+  px_status s = pq_check(h);
+  if (s != PX_OK) return s;
+  if (out == nullptr) return set_error(PX_EINVAL, "out is null");
+  const PqShard& sh = h->shards[0];
+  out->path = 2;
+  out->launches = sh.last_launches;
+  out->fallback_queries = 0;
+  out->profiled = 0;
+  out->main_kernel_ms = 0.f;
+  if (sh.last_profiled) {
+    px::DeviceGuard dg(sh.device);
+    float ms = 0.f;
+    cudaError_t e = cudaEventSynchronize(sh.ev_stop);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, sh.ev_start, sh.ev_stop);
+    if (e != cudaSuccess) return cuda_status(e, "profile events");
+    out->profiled = 1;
+    out->main_kernel_ms = ms;
+  }
+  return PX_OK;
+}
 
 PX_API px_status px_pq_add(px_pq* h, const float* vectors, int64_t n) {
   px_status s = pq_check(h);
