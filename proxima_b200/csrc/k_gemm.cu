@@ -4,22 +4,25 @@
 // The query x base distance matrix is a dense contraction; this kernel
 // computes it tile by tile in TMEM and never writes it to HBM. Operands are
 // the tf32 split planes of the queries and the shard (hi = tf32(x),
-// lo = tf32(x - hi)); each 128 x 256 output tile accumulates
+// lo = tf32(x - hi), interleaved per 16-element chunk); each output tile
+// accumulates
 //     qhi.xhi + qhi.xlo + qlo.xhi            (3xTF32, ~fp32 accurate)
-// and skips a cross term whenever the corresponding lo plane is all zeros
-// (integer-valued data is exact in one pass). The epilogue turns each
+// from 128-byte [hi|lo] TMA rows (128-byte swizzle), skipping a cross term
+// whenever the corresponding lo plane is all zeros. When both lo planes are
+// zero (integer-valued data is exact in one pass) a second variant reads
+// only the 64-byte hi halves (64-byte swizzle). The epilogue turns each
 // accumulator into an approximate key (||x||^2 - 2 q.x for L2, -q.x for
 // inner product) and keeps, per query, the CAP smallest keys in registers.
 // Exactness is restored afterwards: the CAP candidates are rescored in the
 // reference's arithmetic and certified against the error bound of this
 // approximation (k_rescore.cu).
 //
-// CTA roles (192 threads, one CTA per SM):
-//   warp 0      TMA producer: 4-stage ring of {Qhi, Qlo, Xhi, Xlo} K-slices
+// CTA roles (64 + 128*QT threads, one CTA per SM):
+//   warp 0      TMA producer: ring of {QT query tiles, one base tile} K-slices
 //   warp 1      TMEM owner and MMA issuer (one elected thread)
-//   warps 2..5  epilogue: TMEM -> registers -> per-query top-CAP lists
-// Two 256-column fp32 accumulators (all 512 TMEM columns) let the epilogue
-// drain tile t while the tensor core fills tile t+1.
+//   warps 2..   QT epilogue warpgroups: TMEM -> registers -> per-query lists
+// Two accumulator buffers (all 512 TMEM columns) let the epilogue drain tile
+// t while the tensor core fills tile t+1.
 //
 // Work items are (query tile, contiguous run of base tiles); a persistent CTA
 // walks items blockIdx.x, +gridDim.x, ... Items are ordered run-major, so
@@ -37,21 +40,23 @@ namespace px {
 namespace {
 
 constexpr int BM = 128;  // queries per query tile (TMEM lanes)
-constexpr int BK = 16;   // tf32 per stage row: 64 bytes = one 64B swizzle span
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK * 4;  // one plane of one query tile per stage
+constexpr int BK = 16;   // K elements per stage (one 16-element chunk of hi, and of lo)
 constexpr uint32_t kTmemCols = 512;
-constexpr int kNumBars = 2 * STAGES + 2 + 2 + 1;  // full, empty, tmem full, tmem empty, done
 
-// QT query tiles share each base tile of BN(QT) = 256 / QT rows: a stage holds
-// QT x {Qhi, Qlo} and {Xhi, Xlo}, 48 KB for QT = 1 and 2 alike, and the TMEM
-// holds 2 buffers x QT accumulators x BN columns = 512 columns.
-template <int QT> struct Tile {
+// QT query tiles share each base tile of BN = 256 / QT rows. IL (interleaved):
+// a stage row is 128 bytes, [hi x16 | lo x16], 4 stages; hi-only: 64-byte
+// rows, 8 stages. Either way the ring holds 192 KB, and the TMEM holds 2
+// buffers x QT accumulators x BN columns = 512 columns.
+template <int QT, bool IL> struct Tile {
   static constexpr int BN = 256 / QT;
-  static constexpr int B_BYTES = BN * BK * 4;
-  static constexpr int STAGE_BYTES = QT * 2 * A_BYTES + 2 * B_BYTES;
+  static constexpr int ROW = IL ? 128 : 64;  // bytes per tile row per stage
+  static constexpr int STAGES = IL ? 4 : 8;
+  static constexpr int A_TILE = BM * ROW;
+  static constexpr int B_TILE = BN * ROW;
+  static constexpr int STAGE_BYTES = QT * A_TILE + B_TILE;
+  static constexpr int NBARS = 2 * STAGES + 2 + 2 + 1;  // full, empty, tmem full, tmem empty, done
   static constexpr int THREADS = 64 + 128 * QT;  // TMA warp, MMA warp, QT epilogue warpgroups
-  static constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + kNumBars * 8 + 16 + 128 * QT * 33 * 4;
+  static constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + NBARS * 8 + 16 + 128 * QT * 33 * 4;
 };
 
 __device__ __forceinline__ bool mbar_wait_quiet(uint32_t bar, uint32_t parity) {
@@ -96,20 +101,20 @@ __device__ __forceinline__ void list_sort(uint64_t (&L)[CAP]) {
   }
 }
 
-template <int CAP, bool L2, int QT>
-__global__ void __launch_bounds__(Tile<QT>::THREADS, 1)
-gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
-                 const __grid_constant__ CUtensorMap tm_xhi, const __grid_constant__ CUtensorMap tm_xlo,
+template <int CAP, bool L2, int QT, bool IL>
+__global__ void __launch_bounds__(Tile<QT, IL>::THREADS, 1)
+gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_x,
                  const GemmTopkArgs p) {
-  constexpr int BN = Tile<QT>::BN;
-  constexpr int B_BYTES = Tile<QT>::B_BYTES;
-  constexpr int STAGE_BYTES = Tile<QT>::STAGE_BYTES;
-  constexpr int B_OFF = QT * 2 * A_BYTES;  // {Xhi, Xlo} after the QT query tiles
+  using TL = Tile<QT, IL>;
+  constexpr int BN = TL::BN;
+  constexpr int STAGES = TL::STAGES;
+  constexpr int STAGE_BYTES = TL::STAGE_BYTES;
+  constexpr int B_OFF = QT * TL::A_TILE;  // base tile after the QT query tiles
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + TL::NBARS);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
   float* s_keys = reinterpret_cast<float*>(s_tmem + 4);  // (128 * QT) x 33 epilogue key slots
 
@@ -122,8 +127,8 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
   auto tempty_bar = [&](int a) { return tc::smem_addr(&bars[2 * STAGES + 2 + a]); };
   const uint32_t done_bar = tc::smem_addr(&bars[2 * STAGES + 4]);
 
-  const bool q_lo = *p.q_lo_flag != 0;
-  const bool x_lo = p.x_lo_nonzero != 0;
+  const bool q_lo = IL && *p.q_lo_flag != 0;
+  const bool x_lo = IL && p.x_lo_nonzero != 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -139,10 +144,8 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
     tc::fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    tc::prefetch_tmap(&tm_qhi);
-    tc::prefetch_tmap(&tm_xhi);
-    if (q_lo) tc::prefetch_tmap(&tm_qlo);
-    if (x_lo) tc::prefetch_tmap(&tm_xlo);
+    tc::prefetch_tmap(&tm_q);
+    tc::prefetch_tmap(&tm_x);
   }
   if (warp == 1) {
     tc::tmem_alloc(tc::smem_addr(s_tmem), kTmemCols);
@@ -167,7 +170,7 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
         issued[s] = false;
         issued_phase[s] = 0;
       }
-      const uint32_t bytes = QT * A_BYTES * (q_lo ? 2 : 1) + B_BYTES * (x_lo ? 2 : 1);
+      const uint32_t bytes = STAGE_BYTES;
       bool ok = true;
       for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
         const int qp = item % p.T;  // group of QT query tiles
@@ -182,14 +185,11 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
             }
             const uint32_t sbase = smem_base + stage * STAGE_BYTES;
             tc::mbar_arrive_expect_tx(full_bar(stage), bytes);
+            // Chunk kc starts at element 32*kc of an interleaved row.
 #pragma unroll
-            for (int q = 0; q < QT; ++q) {
-              const int qrow = (qp * QT + q) * BM;
-              tc::tma_load_2d(sbase + q * 2 * A_BYTES, &tm_qhi, full_bar(stage), kc * BK, qrow);
-              if (q_lo) tc::tma_load_2d(sbase + q * 2 * A_BYTES + A_BYTES, &tm_qlo, full_bar(stage), kc * BK, qrow);
-            }
-            tc::tma_load_2d(sbase + B_OFF, &tm_xhi, full_bar(stage), kc * BK, t * BN);
-            if (x_lo) tc::tma_load_2d(sbase + B_OFF + B_BYTES, &tm_xlo, full_bar(stage), kc * BK, t * BN);
+            for (int q = 0; q < QT; ++q)
+              tc::tma_load_2d(sbase + q * TL::A_TILE, &tm_q, full_bar(stage), kc * 32, (qp * QT + q) * BM);
+            tc::tma_load_2d(sbase + B_OFF, &tm_x, full_bar(stage), kc * 32, t * BN);
             issued[stage] = true;
             issued_phase[stage] = phase;
             if (++stage == STAGES) {
@@ -230,20 +230,24 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
             }
             tc::tc_fence_after();
             const uint32_t sbase = smem_base + stage * STAGE_BYTES;
-            const uint64_t b_hi = tc::sw64_kmajor_desc(sbase + B_OFF);
-            const uint64_t b_lo = tc::sw64_kmajor_desc(sbase + B_OFF + B_BYTES);
+            const uint64_t b_desc = IL ? tc::sw128_kmajor_desc(sbase + B_OFF) : tc::sw64_kmajor_desc(sbase + B_OFF);
 #pragma unroll
             for (int q = 0; q < QT; ++q) {
               const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((acc * QT + q) * BN);
-              const uint64_t a_hi = tc::sw64_kmajor_desc(sbase + q * 2 * A_BYTES);
-              const uint64_t a_lo = tc::sw64_kmajor_desc(sbase + q * 2 * A_BYTES + A_BYTES);
+              const uint32_t a_addr = sbase + q * TL::A_TILE;
+              const uint64_t a_desc = IL ? tc::sw128_kmajor_desc(a_addr) : tc::sw64_kmajor_desc(a_addr);
 #pragma unroll
               for (int kk = 0; kk < BK / 8; ++kk) {
-                const uint64_t off = static_cast<uint64_t>(kk * 32) >> 4;  // 32 bytes per K step
+                // Descriptor start addresses move in 16-byte units: K step kk
+                // of the hi half sits at 32*kk bytes, of the lo half 64 later.
+                const uint64_t hi = static_cast<uint64_t>(kk * 32) >> 4;
+                const uint64_t lo = static_cast<uint64_t>(64 + kk * 32) >> 4;
                 const uint32_t accumulate = (kc > 0 || kk > 0) ? 1u : 0u;
-                tc::mma_tf32(d_tmem, a_hi + off, b_hi + off, idesc, accumulate);
-                if (x_lo) tc::mma_tf32(d_tmem, a_hi + off, b_lo + off, idesc, 1u);
-                if (q_lo) tc::mma_tf32(d_tmem, a_lo + off, b_hi + off, idesc, 1u);
+                tc::mma_tf32(d_tmem, a_desc + hi, b_desc + hi, idesc, accumulate);
+                if (IL) {
+                  if (x_lo) tc::mma_tf32(d_tmem, a_desc + hi, b_desc + lo, idesc, 1u);
+                  if (q_lo) tc::mma_tf32(d_tmem, a_desc + lo, b_desc + hi, idesc, 1u);
+                }
               }
             }
             tc::mma_commit(empty_bar(stage));
@@ -383,30 +387,35 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-template <int CAP, bool L2, int QT>
+template <int CAP, bool L2, int QT, bool IL>
 cudaError_t launch_typed(const GemmTopkArgs& a, const CUtensorMap* maps, int grid, cudaStream_t stream) {
-  auto kern = gemm_topk_kernel<CAP, L2, QT>;
+  using TL = Tile<QT, IL>;
+  auto kern = gemm_topk_kernel<CAP, L2, QT, IL>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(Tile<QT>::SMEM));
+                                       static_cast<int>(TL::SMEM));
   if (e != cudaSuccess) return e;
-  kern<<<grid, Tile<QT>::THREADS, Tile<QT>::SMEM, stream>>>(maps[0], maps[1], maps[2], maps[3], a);
+  kern<<<grid, TL::THREADS, TL::SMEM, stream>>>(maps[0], maps[1], a);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-// A [rows x ld] fp32 plane as a TMA tensor: boxes of BK (64 bytes) x box_rows,
-// 64-byte swizzle, out-of-range rows read as zeros.
-cudaError_t encode_plane_map(CUtensorMap* map, const float* plane, int64_t rows, int ld, int box_rows) {
+// An interleaved split plane [rows x 2*ld] as a TMA tensor. il: boxes of 32
+// floats (a whole [hi|lo] chunk, 128 bytes, 128-byte swizzle); otherwise 16
+// floats (the hi half, 64 bytes, 64-byte swizzle). Rows past the end read as
+// zeros.
+cudaError_t encode_split_map(CUtensorMap* map, const float* plane, int64_t rows, int ld, int box_rows,
+                             bool il) {
   PFN_cuTensorMapEncodeTiled_v12000 fn = get_encode_fn();
   if (!fn) return cudaErrorNotSupported;
   if (rows < 1) rows = 1;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(ld), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * sizeof(float)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(2 * ld), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(2 * ld) * sizeof(float)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(il ? 32 : 16), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(plane), dims, strides, box,
-                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  il ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
@@ -428,22 +437,28 @@ int gemm_qt_for(int k) { return gemm_cap_for(k) == 32 ? 2 : 1; }
 
 int gemm_bn_for(int k) { return 256 / gemm_qt_for(k); }
 
-cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const float* q_hi, const float* q_lo,
-                             int64_t q_rows, const float* x_hi, const float* x_lo, int grid,
-                             cudaStream_t stream) {
-  if (a.ld % BK != 0) return cudaErrorInvalidValue;
+cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const float* q_hl, int64_t q_rows,
+                             const float* x_hl, bool hi_only, int grid, cudaStream_t stream) {
+  if (a.ld % 32 != 0) return cudaErrorInvalidValue;
   const int qt = gemm_qt_for(a.k);
-  CUtensorMap maps[4];
-  cudaError_t e = encode_plane_map(&maps[0], q_hi, q_rows, a.ld, BM);
-  if (e == cudaSuccess) e = encode_plane_map(&maps[1], q_lo, q_rows, a.ld, BM);
-  if (e == cudaSuccess) e = encode_plane_map(&maps[2], x_hi, a.n, a.ld, 256 / qt);
-  if (e == cudaSuccess) e = encode_plane_map(&maps[3], x_lo, a.n, a.ld, 256 / qt);
+  const bool il = !hi_only;
+  CUtensorMap maps[2];
+  cudaError_t e = encode_split_map(&maps[0], q_hl, q_rows, a.ld, BM, il);
+  if (e == cudaSuccess) e = encode_split_map(&maps[1], x_hl, a.n, a.ld, 256 / qt, il);
   if (e != cudaSuccess) return e;
   const int cap = gemm_cap_for(a.k);
-  if (cap == 32) return a.l2 ? launch_typed<32, true, 2>(a, maps, grid, stream)
-                             : launch_typed<32, false, 2>(a, maps, grid, stream);
-  if (cap == 64) return a.l2 ? launch_typed<64, true, 1>(a, maps, grid, stream)
-                             : launch_typed<64, false, 1>(a, maps, grid, stream);
+  if (cap == 32) {
+    if (il) return a.l2 ? launch_typed<32, true, 2, true>(a, maps, grid, stream)
+                        : launch_typed<32, false, 2, true>(a, maps, grid, stream);
+    return a.l2 ? launch_typed<32, true, 2, false>(a, maps, grid, stream)
+                : launch_typed<32, false, 2, false>(a, maps, grid, stream);
+  }
+  if (cap == 64) {
+    if (il) return a.l2 ? launch_typed<64, true, 1, true>(a, maps, grid, stream)
+                        : launch_typed<64, false, 1, true>(a, maps, grid, stream);
+    return a.l2 ? launch_typed<64, true, 1, false>(a, maps, grid, stream)
+                : launch_typed<64, false, 1, false>(a, maps, grid, stream);
+  }
   return cudaErrorInvalidValue;
 }
 

@@ -4,9 +4,13 @@
 // read them); beside them each row is split for the 3xTF32 contraction:
 //   hi = tf32_rn(x),  lo = tf32_rn(x - hi)      (x - hi is exact in fp32)
 // so that q.x ~= qhi.xhi + qhi.xlo + qlo.xhi with an error of a few 2^-22
-// relative per product. Rows are padded with zeros to a multiple of 32
-// floats, which leaves every dot product unchanged. `norms` holds the squared
-// L2 norm of each row for the approximate key ||x||^2 - 2 q.x.
+// relative per product. The split plane interleaves the two halves per
+// 16-element chunk -- [hi x16 | lo x16], 128 bytes -- so one 128-byte TMA row
+// brings both to shared memory (half the L2 requests of separate planes);
+// a 64-byte box over the same plane reads the hi halves alone. Rows are
+// padded with zeros to a multiple of 32 floats, which leaves every dot
+// product unchanged. `norms` holds the squared L2 norm of each row for the
+// approximate key ||x||^2 - 2 q.x.
 #include "px_common.cuh"
 #include "px_kernels.h"
 
@@ -22,8 +26,8 @@ __device__ __forceinline__ float tf32_rn(float x) {
 
 // One warp per row.
 __global__ void prepare_rows_kernel(const float* __restrict__ src, int64_t n, int d, int ld,
-                                    float* __restrict__ dst, float* __restrict__ hi,
-                                    float* __restrict__ lo, float* __restrict__ norms,
+                                    float* __restrict__ dst, float* __restrict__ hl,
+                                    float* __restrict__ norms,
                                     int* __restrict__ lo_nonzero, int* __restrict__ max_norm_sq) {
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -32,11 +36,12 @@ __global__ void prepare_rows_kernel(const float* __restrict__ src, int64_t n, in
   for (int e = lane; e < ld; e += 32) {
     float x = e < d ? src[row * d + e] : 0.f;
     if (dst) dst[row * ld + e] = x;
-    if (hi) {
-      float h = tf32_rn(x);
-      float l = tf32_rn(__fsub_rn(x, h));
-      hi[row * ld + e] = h;
-      if (lo) lo[row * ld + e] = l;
+    if (hl) {
+      const float h = tf32_rn(x);
+      const float l = tf32_rn(__fsub_rn(x, h));
+      float* r = hl + row * 2 * ld + (e >> 4) * 32 + (e & 15);
+      r[0] = h;
+      r[16] = l;
       nz |= (l != 0.f);
     }
   }
@@ -67,28 +72,25 @@ __global__ void zero_rows_kernel(float* __restrict__ p, int64_t begin, int64_t e
 
 }  // namespace
 
-cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, float* dst, float* hi,
-                                float* lo, float* norms, int* lo_nonzero, int* max_norm_sq,
-                                cudaStream_t stream) {
+cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, float* dst, float* hl,
+                                float* norms, int* lo_nonzero, int* max_norm_sq, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
   const int threads = 256;
   const int64_t blocks = (n * 32 + threads - 1) / threads;
   prepare_rows_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
-      src, n, d, ld, dst, hi, lo, norms, lo_nonzero, max_norm_sq);
+      src, n, d, ld, dst, hl, norms, lo_nonzero, max_norm_sq);
   return cudaGetLastError();
 }
 
 cudaError_t launch_split_queries(const float* q, int64_t nq, int d, int ld, int64_t rows_alloc,
-                                 float* hi, float* lo, float* norms, int* lo_nonzero,
-                                 cudaStream_t stream) {
-  cudaError_t e = launch_prepare_rows(q, nq, d, ld, nullptr, hi, lo, norms, lo_nonzero, nullptr, stream);
+                                 float* hl, int* lo_nonzero, cudaStream_t stream) {
+  cudaError_t e = launch_prepare_rows(q, nq, d, ld, nullptr, hl, nullptr, lo_nonzero, nullptr, stream);
   if (e != cudaSuccess) return e;
   if (rows_alloc > nq) {
-    const int64_t count = (rows_alloc - nq) * ld;
+    const int64_t count = (rows_alloc - nq) * 2 * ld;
     const int threads = 256;
     const unsigned blocks = static_cast<unsigned>((count + threads - 1) / threads);
-    zero_rows_kernel<<<blocks, threads, 0, stream>>>(hi, nq, rows_alloc, ld);
-    if (lo) zero_rows_kernel<<<blocks, threads, 0, stream>>>(lo, nq, rows_alloc, ld);
+    zero_rows_kernel<<<blocks, threads, 0, stream>>>(hl, nq, rows_alloc, 2 * ld);
   }
   return cudaGetLastError();
 }

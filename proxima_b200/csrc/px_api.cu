@@ -179,11 +179,10 @@ px_status FlatShard::ensure_capacity(int64_t need, int ld) {
       new_cap = need;  // drop the growth slack before giving up
     }
   }
-  float *nx = nullptr, *nhi = nullptr, *nlo = nullptr, *nn = nullptr;
+  float *nx = nullptr, *nhl = nullptr, *nn = nullptr;
   const size_t pb = static_cast<size_t>(new_cap) * row_bytes;
   cudaError_t e = cudaMalloc(&nx, pb);
-  if (e == cudaSuccess) e = cudaMalloc(&nhi, pb);
-  if (e == cudaSuccess) e = cudaMalloc(&nlo, pb);
+  if (e == cudaSuccess) e = cudaMalloc(&nhl, 2 * pb);
   // Norms are padded to a whole number of 256-row tiles: the tensor-core
   // epilogue reads them 32 rows at a time, past the last row of a shard.
   const int64_t norm_cap = (new_cap + 255) / 256 * 256;
@@ -192,8 +191,7 @@ px_status FlatShard::ensure_capacity(int64_t need, int ld) {
   if (e != cudaSuccess) {
     cudaGetLastError();
     if (nx) cudaFree(nx);
-    if (nhi) cudaFree(nhi);
-    if (nlo) cudaFree(nlo);
+    if (nhl) cudaFree(nhl);
     if (nn) cudaFree(nn);
     return set_error(PX_ENOMEM, "device allocation of " + std::to_string(new_cap) +
                                     " rows failed on device " + std::to_string(device) + ": " +
@@ -202,18 +200,15 @@ px_status FlatShard::ensure_capacity(int64_t need, int ld) {
   if (n > 0) {
     const size_t used = static_cast<size_t>(n) * row_bytes;
     cudaMemcpyAsync(nx, x, used, cudaMemcpyDeviceToDevice, stream);
-    cudaMemcpyAsync(nhi, hi, used, cudaMemcpyDeviceToDevice, stream);
-    cudaMemcpyAsync(nlo, lo, used, cudaMemcpyDeviceToDevice, stream);
+    cudaMemcpyAsync(nhl, hl, 2 * used, cudaMemcpyDeviceToDevice, stream);
     cudaMemcpyAsync(nn, norms, sizeof(float) * n, cudaMemcpyDeviceToDevice, stream);
     cudaStreamSynchronize(stream);
   }
   if (x) cudaFree(x);
-  if (hi) cudaFree(hi);
-  if (lo) cudaFree(lo);
+  if (hl) cudaFree(hl);
   if (norms) cudaFree(norms);
   x = nx;
-  hi = nhi;
-  lo = nlo;
+  hl = nhl;
   norms = nn;
   cap = new_cap;
   return PX_OK;
@@ -223,10 +218,9 @@ void FlatShard::release() {
   DeviceGuard g(device);
   if (stream) cudaStreamSynchronize(stream);
   if (x) cudaFree(x);
-  if (hi) cudaFree(hi);
-  if (lo) cudaFree(lo);
+  if (hl) cudaFree(hl);
   if (norms) cudaFree(norms);
-  x = hi = lo = norms = nullptr;
+  x = hl = norms = nullptr;
   if (flag) cudaFree(flag);
   flag = nullptr;
   if (ev_start) cudaEventDestroy(ev_start);
@@ -245,8 +239,8 @@ px_status FlatShard::append_device(const float* d_src, int64_t count, int d, int
                                    int64_t global_begin) {
   px_status s = ensure_capacity(n + count, ld);
   if (s != PX_OK) return s;
-  cudaError_t e = launch_prepare_rows(d_src, count, d, ld, x + n * ld, hi + n * ld, lo + n * ld,
-                                      norms + n, flag, flag + 2, stream);
+  cudaError_t e = launch_prepare_rows(d_src, count, d, ld, x + n * ld, hl + n * 2 * ld, norms + n, flag,
+                                      flag + 2, stream);
   if (e != cudaSuccess) return cuda_status(e, "prepare_rows launch");
   segs.local.push_back(n);
   segs.global.push_back(global_begin);

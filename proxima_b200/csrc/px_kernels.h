@@ -88,15 +88,16 @@ cudaError_t launch_nearest_centroid(const float* vectors, int64_t n, int m, int 
 
 // ---- shard preparation (k_prep.cu) ----------------------------------------
 // Copies n rows of d floats into the shard (stride ld, zero padded), and
-// writes the tf32 hi/lo split planes and the squared norms. lo_nonzero is
+// writes the interleaved tf32 split plane `hl` (stride 2*ld: per 16-element
+// chunk 16 hi values then 16 lo values) and the squared norms. lo_nonzero is
 // raised when any lo element is nonzero; max_norm_sq (float bits) is raised
 // to the largest squared norm.
 cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, float* dst,
-                                float* hi, float* lo, float* norms, int* lo_nonzero,
-                                int* max_norm_sq, cudaStream_t stream);
+                                float* hl, float* norms, int* lo_nonzero, int* max_norm_sq,
+                                cudaStream_t stream);
+// Split plane of nq query rows, zero-filled up to rows_alloc rows.
 cudaError_t launch_split_queries(const float* q, int64_t nq, int d, int ld, int64_t rows_alloc,
-                                 float* hi, float* lo, float* norms, int* lo_nonzero,
-                                 cudaStream_t stream);
+                                 float* hl, int* lo_nonzero, cudaStream_t stream);
 
 // ---- K1: tensor-core candidate generation (k_gemm.cu) ---------------------
 struct GemmTopkArgs {
@@ -120,9 +121,10 @@ int gemm_cap_for(int k);    // candidates kept per (query, split) in registers (
 int gemm_cands_for(int k);  // candidates per query after the split merge (<= 256)
 int gemm_qt_for(int k);   // query tiles of 128 per CTA (2 for k <= 16, else 1)
 int gemm_bn_for(int k);   // base rows per tile (256 / qt)
-cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const float* q_hi, const float* q_lo,
-                             int64_t q_rows, const float* x_hi, const float* x_lo, int grid,
-                             cudaStream_t stream);
+// q_hl / x_hl: interleaved split planes (stride 2*ld). hi_only selects the
+// one-pass kernel that reads only the hi halves (both lo planes all zero).
+cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const float* q_hl, int64_t q_rows,
+                             const float* x_hl, bool hi_only, int grid, cudaStream_t stream);
 
 // ---- K5: exact rescoring + certificate (k_rescore.cu) ---------------------
 struct RescoreArgs {

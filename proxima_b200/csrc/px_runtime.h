@@ -62,8 +62,7 @@ struct FlatShard {
   int sms = 148;
   cudaStream_t stream = nullptr;
   float* x = nullptr;      // fp32 rows, stride ld
-  float* hi = nullptr;     // tf32(x)
-  float* lo = nullptr;     // tf32(x - hi)
+  float* hl = nullptr;     // tf32 split, stride 2*ld: per 16-element chunk hi x16 then lo x16
   float* norms = nullptr;  // squared norms
   int64_t n = 0, cap = 0;
   int* flag = nullptr;     // [0] lo plane nonzero, [1] device error code, [2] max squared norm (bits)

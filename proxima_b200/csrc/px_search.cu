@@ -41,7 +41,7 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
                            SearchPlan& plan) {
   plan = SearchPlan{};
   const int cap = gemm_cap_for(k);
-  bool gemm = cap > 0 && !masked && h->ld % 16 == 0 && sh.hi != nullptr;
+  bool gemm = cap > 0 && !masked && h->ld % 32 == 0 && sh.hl != nullptr;
   if (h->path_mode == PX_PATH_EXACT) gemm = false;
   if (h->path_mode == PX_PATH_AUTO) gemm = gemm && nq >= kGemmMinQueries && sh.n >= kGemmMinRows;
   if (h->path_mode == PX_PATH_TENSOR && !gemm)
@@ -71,8 +71,7 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
     plan.n_items = static_cast<int>(T * S);
     plan.grid = static_cast<int>(std::min<int64_t>(sh.sms, T * S));
     plan.q_rows = T * qt * 128;
-    c.take(sizeof(float) * static_cast<size_t>(plan.q_rows) * h->ld);  // q hi
-    c.take(sizeof(float) * static_cast<size_t>(plan.q_rows) * h->ld);  // q lo
+    c.take(sizeof(float) * static_cast<size_t>(plan.q_rows) * 2 * h->ld);  // query split plane
     c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * S * cap);      // split lists
     c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.cands);   // merged
     c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * k);            // final
@@ -149,9 +148,7 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
 
   // ---- tensor-core path ----
   const int cap = plan.cap;
-  const size_t qplane = sizeof(float) * static_cast<size_t>(plan.q_rows) * h->ld;
-  float* q_hi = static_cast<float*>(c.take(qplane));
-  float* q_lo = static_cast<float*>(c.take(qplane));
+  float* q_hl = static_cast<float*>(c.take(sizeof(float) * static_cast<size_t>(plan.q_rows) * 2 * h->ld));
   uint64_t* partial = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.S * cap));
   const int cands = plan.cands;
   uint64_t* merged = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * cands));
@@ -162,9 +159,18 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   const bool l2 = metric == PX_METRIC_L2;
 
   cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int) * 4, stream);
-  if (e == cudaSuccess)
-    e = launch_split_queries(d_q, nq, h->dim, h->ld, plan.q_rows, q_hi, q_lo, nullptr, counters + 1, stream);
+  if (e == cudaSuccess) e = launch_split_queries(d_q, nq, h->dim, h->ld, plan.q_rows, q_hl, counters + 1, stream);
   if (e != cudaSuccess) return cuda_status(e, "query split");
+  // One pass over the hi halves suffices when neither side has a lo part
+  // (e.g. integer-valued data); the query side is known only after the split.
+  bool hi_only = false;
+  if (!sh.lo_nonzero) {
+    int q_lo_host = 1;
+    e = cudaMemcpyAsync(&q_lo_host, counters + 1, sizeof(int), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return cuda_status(e, "query split readback");
+    hi_only = q_lo_host == 0;
+  }
   GemmTopkArgs g;
   g.nq = static_cast<int>(nq);
   g.n = sh.n;
@@ -182,7 +188,7 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   g.partial = partial;
   g.err = sh.flag + 1;
   if (prof) cudaEventRecord(sh.ev_start, stream);
-  e = launch_gemm_topk(g, q_hi, q_lo, plan.q_rows, sh.hi, sh.lo, plan.grid, stream);
+  e = launch_gemm_topk(g, q_hl, plan.q_rows, sh.hl, hi_only, plan.grid, stream);
   if (prof) cudaEventRecord(sh.ev_stop, stream);
   if (e != cudaSuccess) return cuda_status(e, "tensor-core kernel launch");
   e = launch_merge_lists(partial, nq, plan.S, cap, cands, merged, stream);

@@ -170,6 +170,20 @@ __device__ __forceinline__ uint64_t sw64_kmajor_desc(uint32_t saddr) {
   return d;
 }
 
+// The same for a tile written with CU_TENSOR_MAP_SWIZZLE_128B: rows of 128
+// bytes, 8-row groups 1024 bytes apart, layout code 2. The tile must be
+// 1024-byte aligned; the start address moves by 32 bytes per 8-element K
+// step inside the 128-byte row.
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
 // Instruction descriptor: D f32, A/B tf32, both K-major, M x N.
 __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
   return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
