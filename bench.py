@@ -199,9 +199,17 @@ def ncu_traffic(config, kernel):
     return None
 
 
+def host_cores():
+    """Host threads the CPU baseline may use (torchrun sets OMP_NUM_THREADS=1
+    for its workers, so the count is passed to the oracle explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_threads():
-    import oracle
-    return oracle.max_threads()
+    return host_cores()
 
 
 def cpu_sample_qps(base_host, metric, queries_host, k, sample):
@@ -210,7 +218,7 @@ def cpu_sample_qps(base_host, metric, queries_host, k, sample):
     m = O.L2 if metric == "l2" else O.IP
     q = np.ascontiguousarray(queries_host[:sample])
     t = time.perf_counter()
-    ids, d = O.flat_search_batch(base_host, m, q, k, num_threads=0)
+    ids, d = O.flat_search_batch(base_host, m, q, k, num_threads=host_cores())
     dt = time.perf_counter() - t
     return sample / dt, dt, ids, d
 
@@ -316,7 +324,7 @@ def run_pq(args, cfg, rank, world, local_rank):
         codes = pq.encode(base)
         sample = min(args.cpu_sample * 4, nq)
         t = time.perf_counter()
-        ref_ids, ref_d = O.pq_search_batch(books, O.L2, codes, queries[:sample], k, num_threads=0)
+        ref_ids, ref_d = O.pq_search_batch(books, O.L2, codes, queries[:sample], k, num_threads=host_cores())
         dt = time.perf_counter() - t
         cpu = {"value": sample / dt, "unit": "queries/s", "cores": cpu_threads(), "kind": "port",
                "sample": f"first {sample} of the {nq} queries against all {n} codes ({dt:.2f} s); "

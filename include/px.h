@@ -102,6 +102,10 @@ PX_API int64_t px_flat_size(const px_flat* h);
 PX_API int32_t px_flat_dim(const px_flat* h);
 PX_API int32_t px_flat_metric(const px_flat* h);
 
+/* Copies rows [start, start + count) in id order back to the host
+ * (count x dim floats), e.g. to save the index. */
+PX_API px_status px_flat_read_rows(const px_flat* h, int64_t start, int64_t count, float* out);
+
 /* Kernel path for flat searches: AUTO picks the exact streaming scan for
  * small batches (and masks) and the tensor-core path otherwise; EXACT and
  * TENSOR force one (TENSOR fails with PX_EUNSUPPORTED where it cannot serve
@@ -198,6 +202,9 @@ PX_API px_status px_pq_add_codes(px_pq* h, const uint8_t* codes, int64_t n);
 /* ProductQuantizer::encode_into (pq.rs:107-121) for n vectors -> n x m codes. */
 PX_API px_status px_pq_encode(const px_pq* h, const float* vectors, int64_t n, uint8_t* out_codes);
 PX_API int64_t px_pq_size(const px_pq* h);
+/* Copies codes of rows [start, start + count) in id order back to the host
+ * (count x m bytes). */
+PX_API px_status px_pq_read_codes(const px_pq* h, int64_t start, int64_t count, uint8_t* out);
 /* As px_flat_last_profile, for the last PQ search (path = 2, the ADC scan). */
 PX_API px_status px_pq_last_profile(const px_pq* h, px_search_profile* out);
 

@@ -2,8 +2,9 @@
 
 ``from proxima_b200 import FlatIndex, PqIndex, Metric`` gives the classes of
 the reference's ``proxima`` package (python/proxima/__init__.py:1-3) backed
-by sm_100a kernels in libproxima_b200.so. The CPU HNSW index, corpus tooling
-and persistence of the reference are not part of this package.
+by sm_100a kernels in libproxima_b200.so, including the reference's `.sfidx`
+index files (persist.py). The CPU HNSW index and the corpus tooling of the
+reference are not part of this package.
 """
 
 from ._core import FlatIndex, Metric, PqIndex, PX_MAX_K, PxError  # noqa: F401

@@ -112,6 +112,23 @@ class FlatIndex:
         _check_finite(v)
         _lib.check(self._lib.px_flat_add(self._h, _ptr(v, _f32p), v.shape[0]))
 
+    def read_rows(self, start: int, count: int) -> np.ndarray:
+        """Rows [start, start + count) in id order, copied back from the GPU."""
+        out = np.empty((count, self._dim), dtype=np.float32)
+        if count:
+            _lib.check(self._lib.px_flat_read_rows(self._h, start, count, _ptr(out, _f32p)))
+        return out
+
+    # -- lib.rs:219-226 (bincode .sfidx files, see persist.py) -------------
+    def save(self, path) -> None:
+        from .persist import save_flat
+        save_flat(self, os.fspath(path))
+
+    @staticmethod
+    def load(path, *, devices=None) -> "FlatIndex":
+        from .persist import load_flat
+        return load_flat(FlatIndex, os.fspath(path), devices=devices)
+
     def reserve(self, n_total: int) -> None:
         """Pre-sizes device storage for n_total rows (no reallocation on add)."""
         _lib.check(self._lib.px_flat_reserve(self._h, _usize(n_total, "n_total")))
@@ -311,6 +328,25 @@ class PqIndex:
         if c.shape[1] != self._m:
             raise ValueError("code width must equal m")
         _lib.check(self._lib.px_pq_add_codes(self._h, _ptr(c, _u8p), c.shape[0]))
+
+    def read_codes(self, start: int, count: int) -> np.ndarray:
+        """Codes of rows [start, start + count), copied back from the GPU."""
+        self._trained("index is not trained")
+        out = np.empty((count, self._m), dtype=np.uint8)
+        if count:
+            _lib.check(self._lib.px_pq_read_codes(self._h, start, count, _ptr(out, _u8p)))
+        return out
+
+    # -- lib.rs:662-679 (bincode .sfidx files, see persist.py) -------------
+    def save(self, path) -> None:
+        self._trained("index is not trained")
+        from .persist import save_pq
+        save_pq(self, os.fspath(path))
+
+    @staticmethod
+    def load(path, *, devices=None) -> "PqIndex":
+        from .persist import load_pq
+        return load_pq(PqIndex, os.fspath(path), devices=devices)
 
     def encode(self, vectors) -> np.ndarray:
         """ProductQuantizer::encode_into for each row (pq.rs:107-121)."""

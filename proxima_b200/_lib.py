@@ -60,6 +60,8 @@ SIGNATURES = {
     "px_flat_add": (_i32, [_vp, _f32p, _i64]),
     "px_flat_add_device": (_i32, [_vp, _vp, _i64]),
     "px_flat_reserve": (_i32, [_vp, _i64]),
+    "px_flat_read_rows": (_i32, [_vp, _i64, _i64, _f32p]),
+    "px_pq_read_codes": (_i32, [_vp, _i64, _i64, _u8p]),
     "px_flat_size": (_i64, [_vp]),
     "px_flat_dim": (_i32, [_vp]),
     "px_flat_metric": (_i32, [_vp]),

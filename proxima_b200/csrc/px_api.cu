@@ -225,7 +225,8 @@ void FlatShard::release() {
   flag = nullptr;
   if (ev_start) cudaEventDestroy(ev_start);
   if (ev_stop) cudaEventDestroy(ev_stop);
-  ev_start = ev_stop = nullptr;
+  if (ev_done) cudaEventDestroy(ev_done);
+  ev_start = ev_stop = ev_done = nullptr;
   fb.release();
   ws.release();
   stage.release();
@@ -300,6 +301,7 @@ PX_API px_status px_flat_create(int32_t dim, int32_t metric, const int32_t* devi
     if (e == cudaSuccess) e = cudaMemset(sh.flag, 0, 4 * sizeof(int));
     if (e == cudaSuccess) e = cudaEventCreate(&sh.ev_start);
     if (e == cudaSuccess) e = cudaEventCreate(&sh.ev_stop);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sh.ev_done, cudaEventDisableTiming);
     if (e != cudaSuccess) {
       px_status st = cuda_status(e, "create");
       for (auto& x : h->shards) x.release();
@@ -400,6 +402,28 @@ PX_API px_status px_flat_add(px_flat* h, const float* rows, int64_t n) {
     if (s != PX_OK) return s;
   }
   h->total += n;
+  return PX_OK;
+}
+
+PX_API px_status px_flat_read_rows(const px_flat* hc, int64_t start, int64_t count, float* out) {
+  px_status s = flat_check(hc);
+  if (s != PX_OK) return s;
+  if (start < 0 || count < 0 || start + count > hc->total)
+    return set_error(PX_EINVAL, "row range out of bounds");
+  if (count == 0) return PX_OK;
+  if (out == nullptr) return set_error(PX_EINVAL, "out is null");
+  px_flat* h = const_cast<px_flat*>(hc);
+  std::lock_guard<std::mutex> lk(h->mu);
+  for (auto& sh : h->shards) {
+    DeviceGuard dg(sh.device);
+    s = sh.segs.for_range(sh.n, start, start + count, [&](int64_t local, int64_t global, int64_t rows) {
+      cudaError_t e = cudaMemcpy2D(out + (global - start) * h->dim, sizeof(float) * h->dim,
+                                   sh.x + local * h->ld, sizeof(float) * h->ld, sizeof(float) * h->dim,
+                                   static_cast<size_t>(rows), cudaMemcpyDeviceToHost);
+      return cuda_status(e, "row readback");
+    });
+    if (s != PX_OK) return s;
+  }
   return PX_OK;
 }
 
@@ -515,18 +539,18 @@ static px_status flat_search_host(const px_flat* hc, int metric, const float* qu
     if (s != PX_OK) return s;
     for (int g = 0; g < G; ++g) {
       FlatShard& sh = h->shards[g];
-      cudaError_t e = cudaMemcpyPeerAsync(h->gather.ids + g * obytes, s0.device, sh.out_ids,
-                                          sh.device, obytes * sizeof(int64_t), sh.stream);
+      DeviceGuard dgs(sh.device);  // copies and the event go on this shard's own stream
+      cudaError_t e = cudaMemcpyPeerAsync(h->gather.ids + g * obytes, s0.device, sh.out_ids, sh.device,
+                                          obytes * sizeof(int64_t), sh.stream);
       if (e == cudaSuccess)
         e = cudaMemcpyPeerAsync(h->gather.keys + g * obytes, s0.device, sh.out_dists, sh.device,
                                 obytes * sizeof(float), sh.stream);
+      if (e == cudaSuccess && g > 0) e = cudaEventRecord(sh.ev_done, sh.stream);
       if (e != cudaSuccess) return cuda_status(e, "shard gather");
-      if (g > 0) {
-        DeviceGuard dgs(sh.device);
-        e = cudaEventRecord(h->gather.events[g], sh.stream);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(s0.stream, h->gather.events[g], 0);
-        if (e != cudaSuccess) return cuda_status(e, "shard gather sync");
-      }
+    }
+    for (int g = 1; g < G; ++g) {
+      cudaError_t ew = cudaStreamWaitEvent(s0.stream, h->shards[g].ev_done, 0);
+      if (ew != cudaSuccess) return cuda_status(ew, "shard gather wait");
     }
     cudaError_t e = launch_merge_shards(h->gather.keys, h->gather.ids, G, nq, k,
                                         metric == PX_METRIC_L2, natural, h->gather.out_dists,

@@ -49,6 +49,7 @@ struct PqShard {
   int64_t* out_ids = nullptr;
   float* out_dists = nullptr;
   cudaEvent_t ev_start = nullptr, ev_stop = nullptr;  // bracket the scan kernel when profiling
+  cudaEvent_t ev_done = nullptr;  // results copied to the gather buffer (own device)
   bool last_profiled = false;
   int last_launches = 0;
 
@@ -57,7 +58,8 @@ struct PqShard {
     if (stream) cudaStreamSynchronize(stream);
     if (ev_start) cudaEventDestroy(ev_start);
     if (ev_stop) cudaEventDestroy(ev_stop);
-    ev_start = ev_stop = nullptr;
+    if (ev_done) cudaEventDestroy(ev_done);
+    ev_start = ev_stop = ev_done = nullptr;
     if (codes) cudaFree(codes);
     if (books) cudaFree(books);
     codes = nullptr;
@@ -257,18 +259,18 @@ static px_status pq_search_host(const px_pq* hc, const float* queries, int64_t n
     if (s != PX_OK) return s;
     for (int g = 0; g < G; ++g) {
       PqShard& sh = h->shards[g];
+      px::DeviceGuard dgs(sh.device);  // copies and the event go on this shard's own stream
       cudaError_t e = cudaMemcpyPeerAsync(h->gather.ids + g * obytes, s0.device, sh.out_ids, sh.device,
                                           obytes * sizeof(int64_t), sh.stream);
       if (e == cudaSuccess)
         e = cudaMemcpyPeerAsync(h->gather.keys + g * obytes, s0.device, sh.out_dists, sh.device,
                                 obytes * sizeof(float), sh.stream);
+      if (e == cudaSuccess && g > 0) e = cudaEventRecord(sh.ev_done, sh.stream);
       if (e != cudaSuccess) return cuda_status(e, "shard gather");
-      if (g > 0) {
-        px::DeviceGuard dgs(sh.device);
-        e = cudaEventRecord(h->gather.events[g], sh.stream);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(s0.stream, h->gather.events[g], 0);
-        if (e != cudaSuccess) return cuda_status(e, "shard gather sync");
-      }
+    }
+    for (int g = 1; g < G; ++g) {
+      cudaError_t ew = cudaStreamWaitEvent(s0.stream, h->shards[g].ev_done, 0);
+      if (ew != cudaSuccess) return cuda_status(ew, "shard gather wait");
     }
     cudaError_t e = launch_merge_shards(h->gather.keys, h->gather.ids, G, nq, k,
                                         h->metric == PX_METRIC_L2, true, h->gather.out_dists,
@@ -423,6 +425,7 @@ PX_API px_status px_pq_create(int32_t dim, int32_t m, int32_t nbits, int32_t met
     if (e == cudaSuccess) e = cudaMalloc(&sh.books, bb);
     if (e == cudaSuccess) e = cudaEventCreate(&sh.ev_start);
     if (e == cudaSuccess) e = cudaEventCreate(&sh.ev_stop);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sh.ev_done, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaMemcpy(sh.books, h->books.data(), bb, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
       px_status st = cuda_status(e, "PQ create");
@@ -447,6 +450,27 @@ PX_API px_status px_pq_destroy(px_pq* h) {
 }
 
 PX_API int64_t px_pq_size(const px_pq* h) { return h ? h->total : 0; }
+
+PX_API px_status px_pq_read_codes(const px_pq* hc, int64_t start, int64_t count, uint8_t* out) {
+  px_status s = pq_check(hc);
+  if (s != PX_OK) return s;
+  if (start < 0 || count < 0 || start + count > hc->total)
+    return set_error(PX_EINVAL, "row range out of bounds");
+  if (count == 0) return PX_OK;
+  if (out == nullptr) return set_error(PX_EINVAL, "out is null");
+  px_pq* h = const_cast<px_pq*>(hc);
+  std::lock_guard<std::mutex> lk(h->mu);
+  for (auto& sh : h->shards) {
+    px::DeviceGuard dg(sh.device);
+    s = sh.segs.for_range(sh.n, start, start + count, [&](int64_t local, int64_t global, int64_t rows) {
+      cudaError_t e = cudaMemcpy(out + (global - start) * h->m, sh.codes + local * h->m,
+                                 static_cast<size_t>(rows) * h->m, cudaMemcpyDeviceToHost);
+      return cuda_status(e, "code readback");
+    });
+    if (s != PX_OK) return s;
+  }
+  return PX_OK;
+}
 
 PX_API px_status px_pq_last_profile(const px_pq* h, px_search_profile* out) {
   px_status s = pq_check(h);

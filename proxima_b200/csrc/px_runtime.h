@@ -53,6 +53,22 @@ struct Segments {
   px_status sync_device();
   IdSegments view(int64_t id_offset) const;
   void local_mask(const uint8_t* global_mask, int64_t n_local, std::vector<uint8_t>& out) const;
+  // Calls fn(local_begin, global_begin, count) for each run of this shard's
+  // rows whose global ids fall in [start, end).
+  template <class Fn>
+  px_status for_range(int64_t n_local, int64_t start, int64_t end, Fn&& fn) const {
+    for (size_t i = 0; i < local.size(); ++i) {
+      const int64_t lb = local[i];
+      const int64_t le = (i + 1 < local.size()) ? local[i + 1] : n_local;
+      const int64_t gb = global[i], ge = gb + (le - lb);
+      const int64_t s = gb > start ? gb : start, e = ge < end ? ge : end;
+      if (s < e) {
+        px_status st = fn(lb + (s - gb), s, e - s);
+        if (st != PX_OK) return st;
+      }
+    }
+    return PX_OK;
+  }
 };
 
 }  // namespace px
@@ -69,6 +85,7 @@ struct FlatShard {
   bool lo_nonzero = false;
   float max_norm_sq = 0.f;
   cudaEvent_t ev_start = nullptr, ev_stop = nullptr;  // brackets the dominant kernel when profiling
+  cudaEvent_t ev_done = nullptr;  // this shard's results are in the gather buffer (own device)
   int last_path = 0, last_fallback = 0, last_launches = 0;
   bool last_profiled = false;
   px::Segments segs;

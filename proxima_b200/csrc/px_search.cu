@@ -279,8 +279,6 @@ px_status GatherBuf::ensure(int dev, size_t entries) {
   if (e == cudaSuccess) e = cudaMalloc(&ids, entries * sizeof(int64_t));
   if (e == cudaSuccess) e = cudaMalloc(&out_dists, entries * sizeof(float));
   if (e == cudaSuccess) e = cudaMalloc(&out_ids, entries * sizeof(int64_t));
-  for (auto& ev : events)
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
   if (e != cudaSuccess) {
     cudaGetLastError();
     release_all();
@@ -297,10 +295,6 @@ void GatherBuf::release_all() {
     if (ids) cudaFree(ids);
     if (out_dists) cudaFree(out_dists);
     if (out_ids) cudaFree(out_ids);
-    for (auto& ev : events) {
-      if (ev) cudaEventDestroy(ev);
-      ev = nullptr;
-    }
   }
   keys = out_dists = nullptr;
   ids = out_ids = nullptr;
