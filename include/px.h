@@ -107,9 +107,9 @@ PX_API int32_t px_flat_metric(const px_flat* h);
 PX_API px_status px_flat_read_rows(const px_flat* h, int64_t start, int64_t count, float* out);
 
 /* Kernel path for flat searches: AUTO picks the exact streaming scan for
- * small batches (and masks) and the tensor-core path otherwise; EXACT and
+ * small batches and the tensor-core path otherwise; EXACT and
  * TENSOR force one (TENSOR fails with PX_EUNSUPPORTED where it cannot serve
- * the request, e.g. k > 224 or a mask). Results are identical on every path. */
+ * the request, e.g. k > 224). Masks work on both paths. Results are identical on every path. */
 enum { PX_PATH_AUTO = 0, PX_PATH_EXACT = 1, PX_PATH_TENSOR = 2 };
 PX_API px_status px_flat_set_path(px_flat* h, int32_t mode);
 

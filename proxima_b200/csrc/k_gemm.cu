@@ -329,6 +329,7 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 #pragma unroll
           for (int j = 0; j < 32; ++j) pass |= (key[j] <= thr_key ? 1u : 0u) << j;
           if (nvalid < 32) pass &= (1u << nvalid) - 1u;
+          if (p.mask_bits) pass &= __ldg(p.mask_bits + (rbase >> 5));  // rbase is a multiple of 32
           if (pass) {
             // Rare path, one copy of the insertion code: keys go through
             // this thread's shared-memory slot so they can be indexed.

@@ -65,12 +65,30 @@ __global__ void prepare_rows_kernel(const float* __restrict__ src, int64_t n, in
   }
 }
 
+__global__ void pack_mask_kernel(const uint8_t* __restrict__ mask, int64_t n, uint32_t* __restrict__ bits) {
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (w * 32 >= n) return;
+  uint32_t b = 0;
+  for (int j = 0; j < 32; ++j) {
+    const int64_t r = w * 32 + j;
+    if (r < n && mask[r] != 0) b |= 1u << j;
+  }
+  bits[w] = b;
+}
+
 __global__ void zero_rows_kernel(float* __restrict__ p, int64_t begin, int64_t end, int ld) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x + begin * ld;
   if (i < end * ld) p[i] = 0.f;
 }
 
 }  // namespace
+
+cudaError_t launch_pack_mask(const uint8_t* mask, int64_t n, uint32_t* bits, cudaStream_t stream) {
+  const int64_t words = (n + 31) / 32;
+  if (words == 0) return cudaSuccess;
+  pack_mask_kernel<<<static_cast<unsigned>((words + 255) / 256), 256, 0, stream>>>(mask, n, bits);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, float* dst, float* hl,
                                 float* norms, int* lo_nonzero, int* max_norm_sq, cudaStream_t stream) {

@@ -94,7 +94,10 @@ rescore_kernel(const RescoreArgs a) {
     last = m < last ? m : last;
   }
   const uint64_t kth = s_sorted[a.k - 1];
-  if (last != PX_EMPTY && kth != PX_EMPTY) {
+  if (last != PX_EMPTY && kth == PX_EMPTY) {
+    // Fewer than k candidates, yet a full list may hide rows: not certified.
+    ok = 0;
+  } else if (last != PX_EMPTY) {
     const double qn = sqrt(qsq);
     const double xn = static_cast<double>(a.max_norm);
     const bool q_lo = *a.q_lo_flag != 0;

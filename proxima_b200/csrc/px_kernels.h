@@ -116,7 +116,10 @@ struct GemmTopkArgs {
   const int* q_lo_flag; // device word: query lo plane in use
   uint64_t* partial;    // [nq][S][cap] sorted approximate candidates
   int* err;             // device word raised on a timed-out wait
+  const uint32_t* mask_bits;  // optional filter, one bit per row (1 = may be returned)
 };
+// Packs a byte mask (nonzero = keep) into one bit per row, 32 rows per word.
+cudaError_t launch_pack_mask(const uint8_t* mask, int64_t n, uint32_t* bits, cudaStream_t stream);
 int gemm_cap_for(int k);    // candidates kept per (query, split) in registers (0: unsupported)
 int gemm_cands_for(int k);  // candidates per query after the split merge (<= 256)
 int gemm_qt_for(int k);   // query tiles of 128 per CTA (2 for k <= 16, else 1)

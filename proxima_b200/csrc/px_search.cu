@@ -2,8 +2,8 @@
 //
 // Paths:
 //   Exact (K2)  : the exact streaming scan; bit-exact keys, no rescoring.
-//                 Serves small batches (nq < kGemmMinQueries), masks, and
-//                 k beyond the tensor-core path's candidate capacity.
+//                 Serves small batches (nq < kGemmMinQueries) and k beyond
+//                 the tensor-core path's candidate capacity.
 //   Gemm (K1+K5): 3xTF32 tcgen05 contraction with a fused per-query
 //                 top-CAP, split merge, exact rescoring and a certificate;
 //                 queries whose certificate fails are re-run through K2.
@@ -41,7 +41,7 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
                            SearchPlan& plan) {
   plan = SearchPlan{};
   const int cap = gemm_cap_for(k);
-  bool gemm = cap > 0 && !masked && h->ld % 32 == 0 && sh.hl != nullptr;
+  bool gemm = cap > 0 && h->ld % 32 == 0 && sh.hl != nullptr;
   if (h->path_mode == PX_PATH_EXACT) gemm = false;
   if (h->path_mode == PX_PATH_AUTO) gemm = gemm && nq >= kGemmMinQueries && sh.n >= kGemmMinRows;
   if (h->path_mode == PX_PATH_TENSOR && !gemm)
@@ -78,6 +78,7 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
     c.take(sizeof(int) * static_cast<size_t>(nq));                     // status
     c.take(sizeof(int) * static_cast<size_t>(nq));                     // fail list
     c.take(sizeof(int) * 4);                                           // counters
+    if (masked) c.take(sizeof(uint32_t) * static_cast<size_t>((sh.n + 31) / 32 + 8));  // mask bits
   } else {
     plan.path = FlatPath::Exact;
     const int group = exact_group_for(nq);
@@ -156,10 +157,13 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   int* status = static_cast<int*>(c.take(sizeof(int) * static_cast<size_t>(nq)));
   int* fail_list = static_cast<int*>(c.take(sizeof(int) * static_cast<size_t>(nq)));
   int* counters = static_cast<int*>(c.take(sizeof(int) * 4));  // [0] n_fail, [1] q lo flag
+  uint32_t* mask_bits =
+      d_mask ? static_cast<uint32_t*>(c.take(sizeof(uint32_t) * static_cast<size_t>((sh.n + 31) / 32 + 8))) : nullptr;
   const bool l2 = metric == PX_METRIC_L2;
 
   cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int) * 4, stream);
   if (e == cudaSuccess) e = launch_split_queries(d_q, nq, h->dim, h->ld, plan.q_rows, q_hl, counters + 1, stream);
+  if (e == cudaSuccess && mask_bits) e = launch_pack_mask(d_mask, sh.n, mask_bits, stream);
   if (e != cudaSuccess) return cuda_status(e, "query split");
   // One pass over the hi halves suffices when neither side has a lo part
   // (e.g. integer-valued data); the query side is known only after the split.
@@ -187,6 +191,7 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   g.q_lo_flag = counters + 1;
   g.partial = partial;
   g.err = sh.flag + 1;
+  g.mask_bits = mask_bits;
   if (prof) cudaEventRecord(sh.ev_start, stream);
   e = launch_gemm_topk(g, q_hl, plan.q_rows, sh.hl, hi_only, plan.grid, stream);
   if (prof) cudaEventRecord(sh.ev_stop, stream);
@@ -245,7 +250,7 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
     uint64_t* fout = static_cast<uint64_t*>(fc.take(sizeof(uint64_t) * static_cast<size_t>(n_fail) * k));
     e = launch_gather_rows(d_q, h->dim, fail_list, n_fail, fq, stream);
     if (e != cudaSuccess) return cuda_status(e, "fallback gather");
-    s = run_exact(h, sh, metric, fq, n_fail, k, nullptr, fpart, static_cast<int>(ncta), group, rows, fout,
+    s = run_exact(h, sh, metric, fq, n_fail, k, d_mask, fpart, static_cast<int>(ncta), group, rows, fout,
                   stream, false);
     if (s != PX_OK) return s;
     e = launch_scatter_cands(fout, k, fail_list, n_fail, plan.final_cands, stream);

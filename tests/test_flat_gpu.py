@@ -325,5 +325,23 @@ def test_tensor_path_rejects_what_it_cannot_serve(pxm):
     idx.set_search_path("tensor")
     with pytest.raises(pxm.PxError):
         idx.search_batch(O.gen_uniform(32, 16, 2), k=225)
-    with pytest.raises(pxm.PxError):
-        idx.search_batch_filtered(O.gen_uniform(32, 16, 2), np.ones(5000, bool), k=10)
+
+
+@pytest.mark.parametrize("metric", [O.L2, O.IP])
+@pytest.mark.parametrize("k", [10, 100])
+def test_tensor_path_filtered_parity(pxm, metric, k):
+    n, dim, nq = 20000, 64, 48
+    data = _data.unit_gaussian(n, dim, 17)
+    queries = _data.unit_gaussian(nq, dim, 18)
+    idx = pxm.FlatIndex(dim, _metric(pxm, metric))
+    idx.add(data)
+    idx.set_search_path("tensor")
+    rng = np.random.default_rng(k)
+    masks = [rng.random(n) < 0.3,                 # ordinary filter
+             np.arange(n) < 50,                   # all admitted rows in one split
+             (np.arange(n) % 997) == 0,           # fewer than k admitted rows for k=100
+             np.zeros(n, bool)]                   # nothing admitted
+    for mask in masks:
+        ids, d = idx.search_batch_filtered(queries, mask, k=k)
+        assert idx.last_search_profile()["path"] == "tensor"
+        _parity.check_flat(data, metric, queries, ids, d, k, filter_=mask)
