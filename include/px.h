@@ -146,9 +146,14 @@ PX_API px_status px_flat_search_filtered(const px_flat* h, const float* queries,
 
 /* Device-memory variant on a single-device handle: d_queries (nq x dim) and
  * both outputs live on the handle's device; runs on `stream` (a
- * cudaStream_t, NULL = the handle's stream) and returns without
- * synchronising. key_space != 0 writes squared-L2 / -IP keys (the form the
- * cross-shard merge consumes) instead of natural distances. */
+ * cudaStream_t; NULL is CUDA's default stream, as for every `stream`
+ * argument here). The exact path returns without waiting; the tensor-core
+ * path waits on the host for that stream to finish its candidate pass (it
+ * reads back how many queries the certificate sent to the exact scan), then
+ * enqueues the rest. Searches that share a handle share one workspace: keep
+ * them on one stream. key_space != 0
+ * writes squared-L2 / -IP keys (the form the cross-shard merge consumes)
+ * instead of natural distances. */
 PX_API px_status px_flat_search_device(const px_flat* h, const float* d_queries, int64_t nq,
                                        int32_t k, int32_t key_space, int64_t* d_out_ids,
                                        float* d_out_dists, void* stream);

@@ -671,9 +671,11 @@ PX_API px_status px_flat_search_device(const px_flat* hc, const float* d_queries
   std::lock_guard<std::mutex> lk(h->mu);
   FlatShard& sh = h->shards[0];
   DeviceGuard dg(sh.device);
-  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : sh.stream;
+  // NULL is CUDA's default stream, as for every device entry point: torch's
+  // default stream has a null handle, and a search put on any other stream
+  // would not be ordered with the caller's collectives and merges.
   return shard_search(h, sh, h->metric, d_queries, nq, k, nullptr, key_space == 0, d_out_ids,
-                      d_out_dists, st);
+                      d_out_dists, static_cast<cudaStream_t>(stream));
 }
 
 PX_API px_status px_merge_shards_device(int32_t device, const float* d_keys, const int64_t* d_ids,

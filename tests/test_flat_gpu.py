@@ -345,3 +345,38 @@ def test_tensor_path_filtered_parity(pxm, metric, k):
         ids, d = idx.search_batch_filtered(queries, mask, k=k)
         assert idx.last_search_profile()["path"] == "tensor"
         _parity.check_flat(data, metric, queries, ids, d, k, filter_=mask)
+
+
+@pytest.mark.parametrize("path", ["exact", "tensor"])
+@pytest.mark.parametrize("side_stream", [False, True])
+def test_device_search_is_ordered_on_the_callers_stream(pxm, path, side_stream):
+    # The queries are rewritten on the caller's stream behind a ~20 ms spin;
+    # a search that ran on any other stream would read the stale queries.
+    # torch's default stream has a null handle, which must mean CUDA's
+    # default stream (not a private stream of the handle).
+    import torch
+    from proxima_b200 import _lib
+    n, dim, nq, k = 20000, 64, 64, 10
+    data = _data.unit_gaussian(n, dim, 31)
+    q_old = _data.unit_gaussian(nq, dim, 32)
+    q_new = _data.unit_gaussian(nq, dim, 33)
+    idx = pxm.FlatIndex(dim, pxm.Metric.InnerProduct)
+    idx.add(data)
+    idx.set_search_path(path)
+    dev = torch.device("cuda", 0)
+    dq = torch.from_numpy(q_old).to(dev)
+    src = torch.from_numpy(q_new).to(dev)
+    ids = torch.empty((nq, k), dtype=torch.int64, device=dev)
+    dists = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.Stream(dev) if side_stream else torch.cuda.default_stream(dev)
+    assert side_stream or stream.cuda_stream == 0
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(40_000_000)
+        dq.copy_(src)
+        _lib.check(_lib.load().px_flat_search_device(
+            idx.handle, ctypes.c_void_p(dq.data_ptr()), nq, k, 0, ctypes.c_void_p(ids.data_ptr()),
+            ctypes.c_void_p(dists.data_ptr()), ctypes.c_void_p(stream.cuda_stream)))
+    stream.synchronize()
+    assert idx.last_search_profile()["path"] == path
+    _parity.check_flat(data, O.IP, q_new, ids.cpu().numpy(), dists.cpu().numpy(), k)
