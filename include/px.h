@@ -119,9 +119,10 @@ PX_API px_status px_flat_set_path(px_flat* h, int32_t mode);
 typedef struct px_search_profile {
   int32_t path;             /* 0 exact scan, 1 tensor-core path, 2 PQ ADC scan */
   int32_t launches;         /* kernels the search launched on the first shard */
-  int32_t fallback_queries; /* queries re-run by the exact scan (certificate) */
+  int32_t fallback_queries; /* queries the certificate sent to the exact scan */
   int32_t profiled;         /* 1 if main_kernel_ms is valid */
   float main_kernel_ms;     /* device time of the dominant kernel */
+  int32_t refined_queries;  /* queries re-run by the three-pass tensor-core pass */
 } px_search_profile;
 PX_API void px_set_profiling(int32_t enable);
 PX_API px_status px_flat_last_profile(const px_flat* h, px_search_profile* out);
@@ -148,8 +149,8 @@ PX_API px_status px_flat_search_filtered(const px_flat* h, const float* queries,
  * both outputs live on the handle's device; runs on `stream` (a
  * cudaStream_t; NULL is CUDA's default stream, as for every `stream`
  * argument here). The exact path returns without waiting; the tensor-core
- * path waits on the host for that stream to finish its candidate pass (it
- * reads back how many queries the certificate sent to the exact scan), then
+ * path waits on the host for that stream to finish each candidate pass (it
+ * reads back how many queries the certificate left uncertified), then
  * enqueues the rest. Searches that share a handle share one workspace: keep
  * them on one stream. key_space != 0
  * writes squared-L2 / -IP keys (the form the cross-shard merge consumes)

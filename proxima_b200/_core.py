@@ -232,13 +232,14 @@ class FlatIndex:
         _lib.check(self._lib.px_flat_set_path(self._h, self._PATHS[path]))
 
     def last_search_profile(self) -> dict:
-        """Path, kernel launches, certificate fallbacks and (when profiling is
+        """Path, kernel launches, queries the certificate sent to the
+        three-pass refinement and to the exact scan, and (when profiling is
         on, see proxima_b200.set_profiling) the dominant kernel's device time
         of the last search."""
         prof = _lib.SearchProfile()
         _lib.check(self._lib.px_flat_last_profile(self._h, ctypes.byref(prof)))
         return {"path": ("exact", "tensor")[prof.path], "launches": prof.launches,
-                "fallback_queries": prof.fallback_queries,
+                "fallback_queries": prof.fallback_queries, "refined_queries": prof.refined_queries,
                 "main_kernel_ms": prof.main_kernel_ms if prof.profiled else None}
 
 

@@ -256,6 +256,7 @@ void FlatShard::release() {
   if (ev_done) cudaEventDestroy(ev_done);
   ev_start = ev_stop = ev_done = nullptr;
   fb.release();
+  ws2.release();
   ws.release();
   stage.release();
   segs.dev.release();
@@ -379,6 +380,7 @@ PX_API px_status px_flat_last_profile(const px_flat* h, px_search_profile* out) 
   out->path = sh.last_path;
   out->launches = sh.last_launches;
   out->fallback_queries = sh.last_fallback;
+  out->refined_queries = sh.last_refined;
   out->profiled = 0;
   out->main_kernel_ms = 0.f;
   if (sh.last_profiled) {

@@ -125,7 +125,8 @@ int gemm_cands_for(int k);  // candidates per query after the split merge (<= 25
 int gemm_qt_for(int k);   // query tiles of 128 per CTA (2 for k <= 16, else 1)
 int gemm_bn_for(int k);   // base rows per tile (256 / qt)
 // q_hl / x_hl: interleaved split planes (stride 2*ld). hi_only selects the
-// one-pass kernel that reads only the hi halves (both lo planes all zero).
+// one-pass kernel that reads only the hi halves (exact when both lo planes
+// are zero, otherwise within the tf32 bound the certificate accounts for).
 cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const float* q_hl, int64_t q_rows,
                              const float* x_hl, bool hi_only, int grid, cudaStream_t stream);
 
@@ -146,6 +147,7 @@ struct RescoreArgs {
   float max_norm;          // max ||x|| over the shard
   int x_lo_nonzero;
   const int* q_lo_flag;
+  int hi_only;             // the candidate pass used only the hi planes
   uint64_t* out;           // [nq][k] exact candidates
   int* status;             // [nq] 0 = certified
   int* n_fail;             // count of uncertified queries

@@ -90,16 +90,17 @@ struct FlatShard {
   float* hl = nullptr;     // tf32 split, stride 2*ld: per 16-element chunk hi x16 then lo x16
   float* norms = nullptr;  // squared norms
   int64_t n = 0, cap = 0;
-  int* flag = nullptr;     // [0] lo plane nonzero, [1] device error code, [2] max squared norm (bits)
+  int* flag = nullptr;     // [0] lo plane nonzero, [2] max squared norm (bits), written by appends
   bool lo_nonzero = false;
   float max_norm_sq = 0.f;
   cudaEvent_t ev_start = nullptr, ev_stop = nullptr;  // brackets the dominant kernel when profiling
   cudaEvent_t ev_done = nullptr;  // this shard's results are in the gather buffer (own device)
-  int last_path = 0, last_fallback = 0, last_launches = 0;
+  int last_path = 0, last_fallback = 0, last_refined = 0, last_launches = 0;
   bool last_profiled = false;
   px::Segments segs;
   px::DevBuf ws;           // search workspace
   px::DevBuf stage;        // uploads (queries, rows, masks, outputs)
+  px::DevBuf ws2;          // three-pass refinement workspace
   px::DevBuf fb;           // certificate-fallback workspace
   int64_t* out_ids = nullptr;  // results of the last search (inside stage)
   float* out_dists = nullptr;
@@ -161,6 +162,5 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
 px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int metric,
                           const float* d_q, int64_t nq, int k, const uint8_t* d_mask,
                           cudaStream_t stream);
-px_status check_device_flags(FlatShard& sh);
 
 }  // namespace px

@@ -4,9 +4,11 @@
 //   Exact (K2)  : the exact streaming scan; bit-exact keys, no rescoring.
 //                 Serves small batches (nq < kGemmMinQueries) and k beyond
 //                 the tensor-core path's candidate capacity.
-//   Gemm (K1+K5): 3xTF32 tcgen05 contraction with a fused per-query
-//                 top-CAP, split merge, exact rescoring and a certificate;
-//                 queries whose certificate fails are re-run through K2.
+//   Gemm (K1+K5): tcgen05 contraction with a fused per-query top-CAP, split
+//                 merge, exact rescoring and a certificate. The first pass
+//                 reads only the tf32 hi planes; uncertified queries get a
+//                 3xTF32 pass when enough of them fail, and the exact scan
+//                 (K2) serves whatever is still uncertified.
 #include <algorithm>
 #include <atomic>
 #include <cmath>
@@ -37,6 +39,67 @@ int64_t gcd64(int64_t a, int64_t b) {
 
 }  // namespace
 
+// Work split of one tensor-core candidate pass over nq queries.
+static void plan_gemm(const FlatShard& sh, int64_t nq, int k, SearchPlan& plan) {
+  plan.path = FlatPath::Gemm;
+  plan.cap = gemm_cap_for(k);
+  plan.cands = gemm_cands_for(k);
+  // Work items: (group of QT query tiles, run of base tiles of BN rows).
+  const int qt = gemm_qt_for(k);
+  const int bn = gemm_bn_for(k);
+  const int64_t T = ((nq + 127) / 128 + qt - 1) / qt;
+  const int64_t nb = std::max<int64_t>(1, (sh.n + bn - 1) / bn);
+  // Splits so that T * S is a whole number of waves of one CTA per SM.
+  int64_t S = sh.sms / gcd64(T, sh.sms);
+  while (S * 2 <= 1024 && S * T < 2 * sh.sms && S * 2 <= nb) S *= 2;
+  S = std::min<int64_t>(S, nb);
+  S = std::max<int64_t>(S, 1);
+  const int64_t tps = (nb + S - 1) / S;
+  S = (nb + tps - 1) / tps;
+  plan.T = static_cast<int>(T);
+  plan.S = static_cast<int>(S);
+  plan.nb = static_cast<int>(nb);
+  plan.tiles_per_split = static_cast<int>(tps);
+  plan.n_items = static_cast<int>(T * S);
+  plan.grid = static_cast<int>(std::min<int64_t>(sh.sms, T * S));
+  plan.q_rows = T * qt * 128;
+}
+
+namespace {
+
+// Device workspace of one tensor-core candidate pass.
+struct TensorWs {
+  float* q_hl = nullptr;            // query split plane, q_rows x 2*ld
+  uint64_t* partial = nullptr;      // [nq][S][cap] per-split lists
+  uint64_t* merged = nullptr;       // [nq][cands]
+  uint64_t* final_cands = nullptr;  // [nq][k] exact candidates
+  int* status = nullptr;            // [nq]
+  int* fail_list = nullptr;         // [nq] uncertified queries
+  int* counters = nullptr;          // [0] uncertified count, [1] query lo plane in use, [2] timeout
+};
+
+void carve_tensor_ws(Carver& c, const SearchPlan& plan, int64_t nq, int ld, int k, TensorWs& w) {
+  w.q_hl = static_cast<float*>(c.take(sizeof(float) * static_cast<size_t>(plan.q_rows) * 2 * ld));
+  w.partial = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.S * plan.cap));
+  w.merged = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.cands));
+  w.final_cands = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * k));
+  w.status = static_cast<int*>(c.take(sizeof(int) * static_cast<size_t>(nq)));
+  w.fail_list = static_cast<int*>(c.take(sizeof(int) * static_cast<size_t>(nq)));
+  w.counters = static_cast<int*>(c.take(sizeof(int) * 4));
+}
+
+size_t mask_words(int64_t n) { return static_cast<size_t>((n + 31) / 32 + 8); }
+
+// A three-pass candidate pass over the uncertified queries pays when it is
+// cheaper than exact scans of them. Per query, the exact scan issues 2*d
+// FP32 instructions per row (no FMA, reference order) at ~36 T/s, while the
+// three-pass contraction runs at ~186 TFLOP/s of 2*d FLOP per row but over
+// whole groups of 128 * QT queries: the pass pays once the uncertified
+// queries fill about a fifth of one group.
+bool refine_pays(int64_t n_fail, int k) { return n_fail * 5 >= static_cast<int64_t>(gemm_qt_for(k)) * 128; }
+
+}  // namespace
+
 px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, int k, bool masked,
                            SearchPlan& plan) {
   plan = SearchPlan{};
@@ -49,36 +112,10 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
   if (nq > (int64_t(1) << 30)) return set_error(PX_EUNSUPPORTED, "too many queries in one call");
   Carver c;
   if (gemm) {
-    plan.path = FlatPath::Gemm;
-    plan.cap = cap;
-    plan.cands = gemm_cands_for(k);
-    // Work items: (group of QT query tiles, run of base tiles of BN rows).
-    const int qt = gemm_qt_for(k);
-    const int bn = gemm_bn_for(k);
-    const int64_t T = ((nq + 127) / 128 + qt - 1) / qt;
-    const int64_t nb = std::max<int64_t>(1, (sh.n + bn - 1) / bn);
-    // Splits so that T * S is a whole number of waves of one CTA per SM.
-    int64_t S = sh.sms / gcd64(T, sh.sms);
-    while (S * 2 <= 1024 && S * T < 2 * sh.sms && S * 2 <= nb) S *= 2;
-    S = std::min<int64_t>(S, nb);
-    S = std::max<int64_t>(S, 1);
-    const int64_t tps = (nb + S - 1) / S;
-    S = (nb + tps - 1) / tps;
-    plan.T = static_cast<int>(T);
-    plan.S = static_cast<int>(S);
-    plan.nb = static_cast<int>(nb);
-    plan.tiles_per_split = static_cast<int>(tps);
-    plan.n_items = static_cast<int>(T * S);
-    plan.grid = static_cast<int>(std::min<int64_t>(sh.sms, T * S));
-    plan.q_rows = T * qt * 128;
-    c.take(sizeof(float) * static_cast<size_t>(plan.q_rows) * 2 * h->ld);  // query split plane
-    c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * S * cap);      // split lists
-    c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.cands);   // merged
-    c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * k);            // final
-    c.take(sizeof(int) * static_cast<size_t>(nq));                     // status
-    c.take(sizeof(int) * static_cast<size_t>(nq));                     // fail list
-    c.take(sizeof(int) * 4);                                           // counters
-    if (masked) c.take(sizeof(uint32_t) * static_cast<size_t>((sh.n + 31) / 32 + 8));  // mask bits
+    plan_gemm(sh, nq, k, plan);
+    TensorWs w;
+    carve_tensor_ws(c, plan, nq, h->ld, k, w);
+    if (masked) c.take(sizeof(uint32_t) * mask_words(sh.n));
   } else {
     plan.path = FlatPath::Exact;
     const int group = exact_group_for(nq);
@@ -129,52 +166,52 @@ static px_status run_exact(const px_flat* h, FlatShard& sh, int metric, const fl
   return PX_OK;
 }
 
-px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int metric,
-                          const float* d_q, int64_t nq, int k, const uint8_t* d_mask,
-                          cudaStream_t stream) {
-  const bool prof = g_profiling.load() != 0;
-  sh.last_path = static_cast<int>(plan.path);
-  sh.last_fallback = 0;
-  sh.last_profiled = prof;
-  const int64_t launches0 = g_launches.load();
-  Carver c(sh.ws.ptr);
-  if (plan.path == FlatPath::Exact) {
-    plan.partial = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.ncta * k));
-    plan.final_cands = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * k));
-    px_status s = run_exact(h, sh, metric, d_q, nq, k, d_mask, plan.partial, plan.ncta, plan.group,
-                            plan.rows_per_cta, plan.final_cands, stream, prof);
-    sh.last_launches = static_cast<int>(g_launches.load() - launches0);
-    return s;
-  }
+// The exact scan for `count` queries of `src_q` picked by the device list
+// `idx`; their k exact candidates are scattered to dst[idx[j]].
+static px_status exact_for_list(const px_flat* h, FlatShard& sh, int metric, const float* src_q,
+                                const int* idx, int count, int k, const uint8_t* d_mask,
+                                uint64_t* dst, cudaStream_t stream) {
+  const int group = exact_group_for(count);
+  const int64_t groups = (count + group - 1) / group;
+  const int64_t n = std::max<int64_t>(sh.n, 1);
+  int64_t ncta = std::max<int64_t>(1, (static_cast<int64_t>(sh.sms) * 4 + groups - 1) / groups);
+  ncta = std::min<int64_t>(std::min<int64_t>(ncta, (n + 127) / 128), 1024);
+  int64_t rows = ((n + ncta - 1) / ncta + 127) / 128 * 128;
+  ncta = (n + rows - 1) / rows;
+  Carver fc;
+  fc.take(sizeof(float) * static_cast<size_t>(count) * h->dim);
+  fc.take(sizeof(uint64_t) * static_cast<size_t>(count) * ncta * k);
+  fc.take(sizeof(uint64_t) * static_cast<size_t>(count) * k);
+  cudaError_t e = sh.fb.reserve(fc.used);
+  if (e != cudaSuccess) return cuda_status(e, "fallback workspace allocation");
+  fc = Carver(sh.fb.ptr);
+  float* fq = static_cast<float*>(fc.take(sizeof(float) * static_cast<size_t>(count) * h->dim));
+  uint64_t* fpart = static_cast<uint64_t*>(fc.take(sizeof(uint64_t) * static_cast<size_t>(count) * ncta * k));
+  uint64_t* fout = static_cast<uint64_t*>(fc.take(sizeof(uint64_t) * static_cast<size_t>(count) * k));
+  e = launch_gather_rows(src_q, h->dim, idx, count, fq, stream);
+  if (e != cudaSuccess) return cuda_status(e, "fallback gather");
+  px_status s = run_exact(h, sh, metric, fq, count, k, d_mask, fpart, static_cast<int>(ncta), group, rows, fout,
+                          stream, false);
+  if (s != PX_OK) return s;
+  e = launch_scatter_cands(fout, k, idx, count, dst, stream);
+  if (e != cudaSuccess) return cuda_status(e, "fallback scatter");
+  g_launches += 2;
+  return PX_OK;
+}
 
-  // ---- tensor-core path ----
-  const int cap = plan.cap;
-  float* q_hl = static_cast<float*>(c.take(sizeof(float) * static_cast<size_t>(plan.q_rows) * 2 * h->ld));
-  uint64_t* partial = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.S * cap));
-  const int cands = plan.cands;
-  uint64_t* merged = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * cands));
-  plan.final_cands = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * k));
-  int* status = static_cast<int*>(c.take(sizeof(int) * static_cast<size_t>(nq)));
-  int* fail_list = static_cast<int*>(c.take(sizeof(int) * static_cast<size_t>(nq)));
-  int* counters = static_cast<int*>(c.take(sizeof(int) * 4));  // [0] n_fail, [1] q lo flag
-  uint32_t* mask_bits =
-      d_mask ? static_cast<uint32_t*>(c.take(sizeof(uint32_t) * static_cast<size_t>((sh.n + 31) / 32 + 8))) : nullptr;
+// One tensor-core candidate pass: split the queries, K1 over the shard (one
+// pass over the hi planes, or three with the lo planes), split merge, exact
+// rescoring and certificate. Leaves exact candidates in w.final_cands and the
+// uncertified queries in w.fail_list; reads back their count and whether the
+// queries have a lo plane (the one host wait of the pass).
+static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& plan, int metric,
+                             const float* d_q, int64_t nq, int k, const uint32_t* mask_bits,
+                             bool three_pass, const TensorWs& w, bool profile_main, cudaStream_t stream,
+                             int* n_fail, bool* q_lo) {
   const bool l2 = metric == PX_METRIC_L2;
-
-  cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int) * 4, stream);
-  if (e == cudaSuccess) e = launch_split_queries(d_q, nq, h->dim, h->ld, plan.q_rows, q_hl, counters + 1, stream);
-  if (e == cudaSuccess && mask_bits) e = launch_pack_mask(d_mask, sh.n, mask_bits, stream);
+  cudaError_t e = cudaMemsetAsync(w.counters, 0, sizeof(int) * 4, stream);
+  if (e == cudaSuccess) e = launch_split_queries(d_q, nq, h->dim, h->ld, plan.q_rows, w.q_hl, w.counters + 1, stream);
   if (e != cudaSuccess) return cuda_status(e, "query split");
-  // One pass over the hi halves suffices when neither side has a lo part
-  // (e.g. integer-valued data); the query side is known only after the split.
-  bool hi_only = false;
-  if (!sh.lo_nonzero) {
-    int q_lo_host = 1;
-    e = cudaMemcpyAsync(&q_lo_host, counters + 1, sizeof(int), cudaMemcpyDeviceToHost, stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
-    if (e != cudaSuccess) return cuda_status(e, "query split readback");
-    hi_only = q_lo_host == 0;
-  }
   GemmTopkArgs g;
   g.nq = static_cast<int>(nq);
   g.n = sh.n;
@@ -188,24 +225,24 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   g.l2 = l2;
   g.norms = sh.norms;
   g.x_lo_nonzero = sh.lo_nonzero ? 1 : 0;
-  g.q_lo_flag = counters + 1;
-  g.partial = partial;
-  g.err = sh.flag + 1;
+  g.q_lo_flag = w.counters + 1;
+  g.partial = w.partial;
+  g.err = w.counters + 2;
   g.mask_bits = mask_bits;
-  if (prof) cudaEventRecord(sh.ev_start, stream);
-  e = launch_gemm_topk(g, q_hl, plan.q_rows, sh.hl, hi_only, plan.grid, stream);
-  if (prof) cudaEventRecord(sh.ev_stop, stream);
+  if (profile_main) cudaEventRecord(sh.ev_start, stream);
+  e = launch_gemm_topk(g, w.q_hl, plan.q_rows, sh.hl, !three_pass, plan.grid, stream);
+  if (profile_main) cudaEventRecord(sh.ev_stop, stream);
   if (e != cudaSuccess) return cuda_status(e, "tensor-core kernel launch");
-  e = launch_merge_lists(partial, nq, plan.S, cap, cands, merged, stream);
+  e = launch_merge_lists(w.partial, nq, plan.S, plan.cap, plan.cands, w.merged, stream);
   if (e != cudaSuccess) return cuda_status(e, "split merge launch");
   RescoreArgs r;
-  r.merged = merged;
+  r.merged = w.merged;
   r.nq = nq;
-  r.cap = cands;
+  r.cap = plan.cands;
   r.k = k;
-  r.lists = partial;
+  r.lists = w.partial;
   r.nlists = plan.S;
-  r.list_cap = cap;
+  r.list_cap = plan.cap;
   r.queries = d_q;
   r.base = sh.x;
   r.ld = h->ld;
@@ -213,63 +250,101 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   r.l2 = l2;
   r.max_norm = std::sqrt(sh.max_norm_sq);
   r.x_lo_nonzero = sh.lo_nonzero ? 1 : 0;
-  r.q_lo_flag = counters + 1;
-  r.out = plan.final_cands;
-  r.status = status;
-  r.n_fail = counters;
-  r.fail_list = fail_list;
+  r.q_lo_flag = w.counters + 1;
+  r.hi_only = three_pass ? 0 : 1;
+  r.out = w.final_cands;
+  r.status = w.status;
+  r.n_fail = w.counters;
+  r.fail_list = w.fail_list;
   e = launch_rescore(r, stream);
   if (e != cudaSuccess) return cuda_status(e, "rescore launch");
   g_launches += 5;  // split, gemm, merge, rescore (+ memset counted as one)
-
-  // Certificate failures: re-run those queries through the exact scan.
-  int n_fail = 0;
-  e = cudaMemcpyAsync(&n_fail, counters, sizeof(int), cudaMemcpyDeviceToHost, stream);
+  int hc[3] = {0, 0, 0};
+  e = cudaMemcpyAsync(hc, w.counters, sizeof(hc), cudaMemcpyDeviceToHost, stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
   if (e != cudaSuccess) return cuda_status(e, "certificate readback");
-  px_status s = check_device_flags(sh);
-  if (s != PX_OK) return s;
-  sh.last_fallback = n_fail;
-  if (n_fail > 0) {
-    const int group = exact_group_for(n_fail);
-    const int64_t groups = (n_fail + group - 1) / group;
-    const int64_t n = std::max<int64_t>(sh.n, 1);
-    int64_t ncta = std::max<int64_t>(1, (static_cast<int64_t>(sh.sms) * 4 + groups - 1) / groups);
-    ncta = std::min<int64_t>(std::min<int64_t>(ncta, (n + 127) / 128), 1024);
-    int64_t rows = ((n + ncta - 1) / ncta + 127) / 128 * 128;
-    ncta = (n + rows - 1) / rows;
-    Carver fc;
-    fc.take(sizeof(float) * static_cast<size_t>(n_fail) * h->dim);
-    fc.take(sizeof(uint64_t) * static_cast<size_t>(n_fail) * ncta * k);
-    fc.take(sizeof(uint64_t) * static_cast<size_t>(n_fail) * k);
-    e = sh.fb.reserve(fc.used);
-    if (e != cudaSuccess) return cuda_status(e, "fallback workspace allocation");
-    fc = Carver(sh.fb.ptr);
-    float* fq = static_cast<float*>(fc.take(sizeof(float) * static_cast<size_t>(n_fail) * h->dim));
-    uint64_t* fpart = static_cast<uint64_t*>(fc.take(sizeof(uint64_t) * static_cast<size_t>(n_fail) * ncta * k));
-    uint64_t* fout = static_cast<uint64_t*>(fc.take(sizeof(uint64_t) * static_cast<size_t>(n_fail) * k));
-    e = launch_gather_rows(d_q, h->dim, fail_list, n_fail, fq, stream);
-    if (e != cudaSuccess) return cuda_status(e, "fallback gather");
-    s = run_exact(h, sh, metric, fq, n_fail, k, d_mask, fpart, static_cast<int>(ncta), group, rows, fout,
-                  stream, false);
-    if (s != PX_OK) return s;
-    e = launch_scatter_cands(fout, k, fail_list, n_fail, plan.final_cands, stream);
-    if (e != cudaSuccess) return cuda_status(e, "fallback scatter");
-    g_launches += 2;
-  }
-  sh.last_launches = static_cast<int>(g_launches.load() - launches0);
+  if (hc[2] != 0)
+    return set_error(PX_ETIMEOUT, "a tensor-core pipeline wait timed out on device " +
+                                      std::to_string(sh.device) + "; the search was abandoned");
+  *n_fail = hc[0];
+  *q_lo = hc[1] != 0;
   return PX_OK;
 }
 
-px_status check_device_flags(FlatShard& sh) {
-  int err = 0;
-  cudaError_t e = cudaMemcpy(&err, sh.flag + 1, sizeof(int), cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return cuda_status(e, "device status readback");
-  if (err != 0) {
-    cudaMemset(sh.flag + 1, 0, sizeof(int));
-    return set_error(PX_ETIMEOUT, "a tensor-core pipeline wait timed out on device " +
-                                      std::to_string(sh.device) + "; the search was abandoned");
+px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int metric,
+                          const float* d_q, int64_t nq, int k, const uint8_t* d_mask,
+                          cudaStream_t stream) {
+  const bool prof = g_profiling.load() != 0;
+  sh.last_path = static_cast<int>(plan.path);
+  sh.last_fallback = 0;
+  sh.last_refined = 0;
+  sh.last_profiled = prof;
+  const int64_t launches0 = g_launches.load();
+  Carver c(sh.ws.ptr);
+  if (plan.path == FlatPath::Exact) {
+    plan.partial = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.ncta * k));
+    plan.final_cands = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * k));
+    px_status s = run_exact(h, sh, metric, d_q, nq, k, d_mask, plan.partial, plan.ncta, plan.group,
+                            plan.rows_per_cta, plan.final_cands, stream, prof);
+    sh.last_launches = static_cast<int>(g_launches.load() - launches0);
+    return s;
   }
+
+  // ---- tensor-core path ----
+  // 1. One pass over the hi planes for every query. Its keys carry a tf32
+  //    rounding error, which the certificate's bound covers; on typical
+  //    data nearly every query is certified.
+  // 2. The uncertified queries, if the lo planes are in use and there are
+  //    enough of them, get a three-pass (~fp32) candidate pass.
+  // 3. Whatever is still uncertified goes through the exact scan.
+  TensorWs w;
+  carve_tensor_ws(c, plan, nq, h->ld, k, w);
+  plan.final_cands = w.final_cands;
+  uint32_t* mask_bits = d_mask ? static_cast<uint32_t*>(c.take(sizeof(uint32_t) * mask_words(sh.n))) : nullptr;
+  if (mask_bits) {
+    cudaError_t e = launch_pack_mask(d_mask, sh.n, mask_bits, stream);
+    if (e != cudaSuccess) return cuda_status(e, "mask pack");
+  }
+  int n_fail = 0;
+  bool q_lo = false;
+  px_status s = tensor_pass(h, sh, plan, metric, d_q, nq, k, mask_bits, false, w, prof, stream, &n_fail, &q_lo);
+  if (s != PX_OK) return s;
+  if (n_fail > 0) {
+    const bool lo_used = sh.lo_nonzero || q_lo;
+    if (lo_used && refine_pays(n_fail, k)) {
+      SearchPlan p2;
+      plan_gemm(sh, n_fail, k, p2);
+      Carver c2;
+      c2.take(sizeof(float) * static_cast<size_t>(n_fail) * h->dim);
+      TensorWs w2;
+      carve_tensor_ws(c2, p2, n_fail, h->ld, k, w2);
+      cudaError_t e = sh.ws2.reserve(c2.used);
+      if (e != cudaSuccess) return cuda_status(e, "refinement workspace allocation");
+      c2 = Carver(sh.ws2.ptr);
+      float* fq = static_cast<float*>(c2.take(sizeof(float) * static_cast<size_t>(n_fail) * h->dim));
+      carve_tensor_ws(c2, p2, n_fail, h->ld, k, w2);
+      e = launch_gather_rows(d_q, h->dim, w.fail_list, n_fail, fq, stream);
+      if (e != cudaSuccess) return cuda_status(e, "refinement gather");
+      int n_fail2 = 0;
+      bool q_lo2 = false;
+      s = tensor_pass(h, sh, p2, metric, fq, n_fail, k, mask_bits, true, w2, false, stream, &n_fail2, &q_lo2);
+      if (s != PX_OK) return s;
+      if (n_fail2 > 0) {
+        s = exact_for_list(h, sh, metric, fq, w2.fail_list, n_fail2, k, d_mask, w2.final_cands, stream);
+        if (s != PX_OK) return s;
+      }
+      e = launch_scatter_cands(w2.final_cands, k, w.fail_list, n_fail, w.final_cands, stream);
+      if (e != cudaSuccess) return cuda_status(e, "refinement scatter");
+      g_launches += 2;
+      sh.last_refined = n_fail;
+      sh.last_fallback = n_fail2;
+    } else {
+      s = exact_for_list(h, sh, metric, d_q, w.fail_list, n_fail, k, d_mask, w.final_cands, stream);
+      if (s != PX_OK) return s;
+      sh.last_fallback = n_fail;
+    }
+  }
+  sh.last_launches = static_cast<int>(g_launches.load() - launches0);
   return PX_OK;
 }
 

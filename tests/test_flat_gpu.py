@@ -284,8 +284,10 @@ def test_tensor_path_parity(pxm, metric, n, dim, nq, k):
     ids, d, prof = _run_path(pxm, data, metric, queries, k, "tensor")
     assert prof["path"] == "tensor"
     _parity.check_flat(data, metric, queries, ids, d, k)
-    # Fallbacks are legal but must stay rare on generic data.
-    assert prof["fallback_queries"] <= max(2, nq // 20), prof
+    # Exact-scan fallbacks are legal but must stay rare on generic data
+    # (clustered L2 data leaves a few percent uncertified by the one-pass
+    # candidates when too few fail for the three-pass refinement to pay).
+    assert prof["fallback_queries"] <= max(4, nq // 10), prof
 
 
 def test_tensor_path_integer_data_single_pass(pxm):
@@ -380,3 +382,25 @@ def test_device_search_is_ordered_on_the_callers_stream(pxm, path, side_stream):
     stream.synchronize()
     assert idx.last_search_profile()["path"] == path
     _parity.check_flat(data, O.IP, q_new, ids.cpu().numpy(), dists.cpu().numpy(), k)
+
+
+@pytest.mark.parametrize("metric", [O.L2, O.IP])
+def test_tensor_path_three_tiers(pxm, metric):
+    # Every row comes in 48 copies perturbed by 2e-4 per coordinate, so more
+    # than the 32 candidates a list keeps sit within ~3e-4 of each other:
+    # the one-pass bound (~1e-3) cannot certify them, the three-pass bound
+    # (~2e-5) can. With 256 queries the three-pass refinement pays, and the
+    # exact scan sees at most the few queries that are still uncertified.
+    rng = np.random.default_rng(5)
+    base = _data.unit_gaussian(800, 96, 6)
+    data = np.repeat(base, 48, axis=0)
+    data = (data + rng.standard_normal(data.shape).astype(np.float32) * np.float32(2e-4)).astype(np.float32)
+    queries = _data.unit_gaussian(256, 96, 7)
+    ids, d, prof = _run_path(pxm, data, metric, queries, 10, "tensor")
+    _parity.check_flat(data, metric, queries, ids, d, 10)
+    assert prof["refined_queries"] >= 200, prof
+    assert prof["fallback_queries"] <= prof["refined_queries"] // 4, prof
+    # Few uncertified queries go straight to the exact scan.
+    ids, d, prof = _run_path(pxm, data, metric, queries[:20], 10, "tensor")
+    _parity.check_flat(data, metric, queries[:20], ids, d, 10)
+    assert prof["refined_queries"] == 0 and prof["fallback_queries"] > 0, prof
