@@ -465,16 +465,22 @@ def run_ours(args, cfg, rank, world, local_rank):
         if path == "tensor":
             flops = 2.0 * nq * n_local * dim
             achieved = flops / avg_s / 1e12
-            peak = pk["bf16_tflops_sustained"] / 2.0
+            first = index.local.last_search_profile()["first_pass"]
+            # bf16 MMAs issue at the measured bf16 rate, tf32 at half of it.
+            peak = pk["bf16_tflops_sustained"] / (1.0 if first == "bf16" else 2.0)
             traffic = ncu_traffic(args.config, "gemm_topk_kernel") if world == 1 else None
             roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                         "frac": achieved / peak, "traffic": traffic,
                         "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
                                         "(profiles/gemm_topk_kernel.md)" if traffic else None,
-                        "kernel": "gemm_topk_kernel (tcgen05 kind::tf32, one pass over the hi planes)",
+                        "kernel": "gemm_topk_kernel (tcgen05 " + ("kind::f16, bf16 operands"
+                                                                  if first == "bf16" else
+                                                                  "kind::tf32, hi values") + ")",
                         "kernel_ms": statistics.mean(kernel_ms),
-                        "peak_basis": f"TF32 rate = bf16_tflops_sustained {pk['bf16_tflops_sustained']} "
-                                      f"/ 2 (tf32 MMA rate), {pk['source']}",
+                        "peak_basis": (f"bf16 rate = bf16_tflops_sustained {pk['bf16_tflops_sustained']}, "
+                                       if first == "bf16" else
+                                       f"TF32 rate = bf16_tflops_sustained {pk['bf16_tflops_sustained']} "
+                                       f"/ 2 (tf32 MMA rate), ") + pk["source"],
                         "frac_of_bf16_peak": achieved / pk["bf16_tflops_sustained"],
                         "algorithmic_flops_per_launch": flops}
         else:

@@ -123,6 +123,8 @@ typedef struct px_search_profile {
   int32_t profiled;         /* 1 if main_kernel_ms is valid */
   float main_kernel_ms;     /* device time of the dominant kernel */
   int32_t refined_queries;  /* queries re-run by the three-pass tensor-core pass */
+  int32_t first_pass;       /* tensor-core path: operands of the first candidate
+                               pass, 0 three-pass tf32, 1 tf32, 2 bf16; else -1 */
 } px_search_profile;
 PX_API void px_set_profiling(int32_t enable);
 PX_API px_status px_flat_last_profile(const px_flat* h, px_search_profile* out);

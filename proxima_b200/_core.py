@@ -240,6 +240,7 @@ class FlatIndex:
         _lib.check(self._lib.px_flat_last_profile(self._h, ctypes.byref(prof)))
         return {"path": ("exact", "tensor")[prof.path], "launches": prof.launches,
                 "fallback_queries": prof.fallback_queries, "refined_queries": prof.refined_queries,
+                "first_pass": {0: "3xtf32", 1: "tf32", 2: "bf16"}.get(prof.first_pass),
                 "main_kernel_ms": prof.main_kernel_ms if prof.profiled else None}
 
 

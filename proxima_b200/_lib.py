@@ -45,7 +45,8 @@ class SearchProfile(ctypes.Structure):
     """px_search_profile (include/px.h)."""
     _fields_ = [("path", ctypes.c_int32), ("launches", ctypes.c_int32),
                 ("fallback_queries", ctypes.c_int32), ("profiled", ctypes.c_int32),
-                ("main_kernel_ms", ctypes.c_float), ("refined_queries", ctypes.c_int32)]
+                ("main_kernel_ms", ctypes.c_float), ("refined_queries", ctypes.c_int32),
+                ("first_pass", ctypes.c_int32)]
 
 
 SIGNATURES = {

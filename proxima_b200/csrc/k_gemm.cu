@@ -8,9 +8,12 @@
 // accumulates
 //     qhi.xhi + qhi.xlo + qlo.xhi            (3xTF32, ~fp32 accurate)
 // from 128-byte [hi|lo] TMA rows (128-byte swizzle), skipping a cross term
-// whenever the corresponding lo plane is all zeros. When both lo planes are
-// zero (integer-valued data is exact in one pass) a second variant reads
-// only the 64-byte hi halves (64-byte swizzle). The epilogue turns each
+// whenever the corresponding lo plane is all zeros. A second variant reads
+// only the 64-byte hi halves (64-byte swizzle) and multiplies qhi.xhi, and a
+// third multiplies the bf16 copies of queries and rows (kind::f16, 128-byte
+// rows of 64 elements) at twice the tf32 rate and half the bytes; both are
+// exact for integer-valued data and otherwise carry a rounding error the
+// certificate accounts for. The epilogue turns each
 // accumulator into an approximate key (||x||^2 - 2 q.x for L2, -q.x for
 // inner product) and keeps, per query, the CAP smallest keys in registers.
 // Exactness is restored afterwards: the CAP candidates are rescored in the
@@ -40,17 +43,21 @@ namespace px {
 namespace {
 
 constexpr int BM = 128;  // queries per query tile (TMEM lanes)
-constexpr int BK = 16;   // K elements per stage (one 16-element chunk of hi, and of lo)
 constexpr uint32_t kTmemCols = 512;
 
-// QT query tiles share each base tile of BN = 256 / QT rows. IL (interleaved):
-// a stage row is 128 bytes, [hi x16 | lo x16], 4 stages; hi-only: 64-byte
-// rows, 8 stages. Either way the ring holds 192 KB, and the TMEM holds 2
-// buffers x QT accumulators x BN columns = 512 columns.
-template <int QT, bool IL> struct Tile {
+// QT query tiles share each base tile of BN = 256 / QT rows. A stage row is
+// 128 bytes -- [hi x16 | lo x16] tf32 (3xTF32) or 64 bf16 values -- with 4
+// stages, or 64 bytes of hi values with 8 stages (tf32 hi-only). Either way
+// the ring holds 192 KB, and the TMEM holds 2 buffers x QT accumulators x BN
+// columns = 512 columns.
+template <int QT, int KIND> struct Tile {
+  static constexpr bool IL = KIND == kPass3xTf32;
+  static constexpr bool BF = KIND == kPassBf16;
   static constexpr int BN = 256 / QT;
-  static constexpr int ROW = IL ? 128 : 64;  // bytes per tile row per stage
-  static constexpr int STAGES = IL ? 4 : 8;
+  static constexpr int ROW = KIND == kPassTf32 ? 64 : 128;  // bytes per tile row per stage
+  static constexpr int STAGES = KIND == kPassTf32 ? 8 : 4;
+  static constexpr int KEL = BF ? 64 : 16;    // K elements per stage
+  static constexpr int KCOORD = BF ? 64 : 32; // plane columns per stage
   static constexpr int A_TILE = BM * ROW;
   static constexpr int B_TILE = BN * ROW;
   static constexpr int STAGE_BYTES = QT * A_TILE + B_TILE;
@@ -62,6 +69,24 @@ template <int QT, bool IL> struct Tile {
 __device__ __forceinline__ bool mbar_wait_quiet(uint32_t bar, uint32_t parity) {
   int dummy = 0;
   return tc::mbar_wait(bar, parity, &dummy);
+}
+
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+  float r;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Smallest of 32 keys: a depth-4 tree of three-input minimums (16 ops).
+__device__ __forceinline__ float min32(const float (&k)[32]) {
+  float a[10];
+#pragma unroll
+  for (int i = 0; i < 10; ++i) a[i] = min3f(k[3 * i], k[3 * i + 1], k[3 * i + 2]);
+  const float b0 = min3f(a[0], a[1], a[2]);
+  const float b1 = min3f(a[3], a[4], a[5]);
+  const float b2 = min3f(a[6], a[7], a[8]);
+  const float b3 = min3f(a[9], k[30], k[31]);
+  return fminf(min3f(b0, b1, b2), b3);
 }
 
 template <int CAP>
@@ -101,11 +126,13 @@ __device__ __forceinline__ void list_sort(uint64_t (&L)[CAP]) {
   }
 }
 
-template <int CAP, bool L2, int QT, bool IL>
-__global__ void __launch_bounds__(Tile<QT, IL>::THREADS, 1)
+template <int CAP, bool L2, int QT, int KIND>
+__global__ void __launch_bounds__(Tile<QT, KIND>::THREADS, 1)
 gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_x,
                  const GemmTopkArgs p) {
-  using TL = Tile<QT, IL>;
+  using TL = Tile<QT, KIND>;
+  constexpr bool IL = TL::IL;
+  constexpr bool SW128 = KIND != kPassTf32;
   constexpr int BN = TL::BN;
   constexpr int STAGES = TL::STAGES;
   constexpr int STAGE_BYTES = TL::STAGE_BYTES;
@@ -156,7 +183,7 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   tc::tc_fence_after();
   const uint32_t tmem_base = *s_tmem;
 
-  const int KC = p.ld / BK;
+  const int KC = TL::BF ? p.ldb / TL::KEL : p.ld / TL::KEL;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -185,11 +212,13 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             }
             const uint32_t sbase = smem_base + stage * STAGE_BYTES;
             tc::mbar_arrive_expect_tx(full_bar(stage), bytes);
-            // Chunk kc starts at element 32*kc of an interleaved row.
+            // Slice kc starts at column 32*kc of an interleaved tf32 row, or
+            // 64*kc of a bf16 row.
 #pragma unroll
             for (int q = 0; q < QT; ++q)
-              tc::tma_load_2d(sbase + q * TL::A_TILE, &tm_q, full_bar(stage), kc * 32, (qp * QT + q) * BM);
-            tc::tma_load_2d(sbase + B_OFF, &tm_x, full_bar(stage), kc * 32, t * BN);
+              tc::tma_load_2d(sbase + q * TL::A_TILE, &tm_q, full_bar(stage), kc * TL::KCOORD,
+                              (qp * QT + q) * BM);
+            tc::tma_load_2d(sbase + B_OFF, &tm_x, full_bar(stage), kc * TL::KCOORD, t * BN);
             issued[stage] = true;
             issued_phase[stage] = phase;
             if (++stage == STAGES) {
@@ -207,7 +236,7 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = tc::idesc_tf32(BM, BN);
+      constexpr uint32_t idesc = TL::BF ? tc::idesc_bf16(BM, BN) : tc::idesc_tf32(BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -230,23 +259,33 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             }
             tc::tc_fence_after();
             const uint32_t sbase = smem_base + stage * STAGE_BYTES;
-            const uint64_t b_desc = IL ? tc::sw128_kmajor_desc(sbase + B_OFF) : tc::sw64_kmajor_desc(sbase + B_OFF);
+            const uint64_t b_desc =
+                SW128 ? tc::sw128_kmajor_desc(sbase + B_OFF) : tc::sw64_kmajor_desc(sbase + B_OFF);
 #pragma unroll
             for (int q = 0; q < QT; ++q) {
               const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((acc * QT + q) * BN);
               const uint32_t a_addr = sbase + q * TL::A_TILE;
-              const uint64_t a_desc = IL ? tc::sw128_kmajor_desc(a_addr) : tc::sw64_kmajor_desc(a_addr);
+              const uint64_t a_desc = SW128 ? tc::sw128_kmajor_desc(a_addr) : tc::sw64_kmajor_desc(a_addr);
+              if constexpr (TL::BF) {
+                // Four K steps of 16 bf16 values (32 bytes) per 128-byte row.
 #pragma unroll
-              for (int kk = 0; kk < BK / 8; ++kk) {
-                // Descriptor start addresses move in 16-byte units: K step kk
-                // of the hi half sits at 32*kk bytes, of the lo half 64 later.
-                const uint64_t hi = static_cast<uint64_t>(kk * 32) >> 4;
-                const uint64_t lo = static_cast<uint64_t>(64 + kk * 32) >> 4;
-                const uint32_t accumulate = (kc > 0 || kk > 0) ? 1u : 0u;
-                tc::mma_tf32(d_tmem, a_desc + hi, b_desc + hi, idesc, accumulate);
-                if (IL) {
-                  if (x_lo) tc::mma_tf32(d_tmem, a_desc + hi, b_desc + lo, idesc, 1u);
-                  if (q_lo) tc::mma_tf32(d_tmem, a_desc + lo, b_desc + hi, idesc, 1u);
+                for (int kk = 0; kk < 4; ++kk) {
+                  const uint64_t off = static_cast<uint64_t>(kk * 32) >> 4;
+                  tc::mma_bf16(d_tmem, a_desc + off, b_desc + off, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+                }
+              } else {
+#pragma unroll
+                for (int kk = 0; kk < 2; ++kk) {
+                  // Descriptor start addresses move in 16-byte units: K step kk
+                  // of the hi half sits at 32*kk bytes, of the lo half 64 later.
+                  const uint64_t hi = static_cast<uint64_t>(kk * 32) >> 4;
+                  const uint64_t lo = static_cast<uint64_t>(64 + kk * 32) >> 4;
+                  const uint32_t accumulate = (kc > 0 || kk > 0) ? 1u : 0u;
+                  tc::mma_tf32(d_tmem, a_desc + hi, b_desc + hi, idesc, accumulate);
+                  if (IL) {
+                    if (x_lo) tc::mma_tf32(d_tmem, a_desc + hi, b_desc + lo, idesc, 1u);
+                    if (q_lo) tc::mma_tf32(d_tmem, a_desc + lo, b_desc + hi, idesc, 1u);
+                  }
                 }
               }
             }
@@ -291,7 +330,8 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       int maxpos = 0;
       for (int t = t0; t < t1; ++t) {
         // Warp-uniform decision: the tcgen05.ld below is .sync.aligned.
-        const bool got = __all_sync(0xffffffffu, tc::mbar_wait(tfull_bar(acc), acc_phase, s_abort));
+        // Tiles take microseconds: poll every ~256 ns.
+        const bool got = __all_sync(0xffffffffu, tc::mbar_wait(tfull_bar(acc), acc_phase, s_abort, 256));
         if (!got) {
           ok = false;
           break;
@@ -303,13 +343,14 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         const uint32_t col0 = static_cast<uint32_t>((acc * QT + wg) * BN);
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
+          __syncwarp();  // the tcgen05.ld below is .sync.aligned
           uint32_t v[32];
           tc::tmem_ld_32x32b_x32(lane_addr + col0 + static_cast<uint32_t>(c * 32), v);
           tc::tmem_ld_wait();
           const int64_t rbase = row0 + c * 32;
           const int nvalid = valid_cols - c * 32;
           if (nvalid <= 0) continue;
-          // Hot path: keys and a bit mask of those that beat the threshold.
+          // Hot path: the approximate keys of 32 columns.
           float key[32];
           if (L2) {
             const float4* nrm = reinterpret_cast<const float4*>(p.norms + rbase);
@@ -325,6 +366,10 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 #pragma unroll
             for (int j = 0; j < 32; ++j) key[j] = -__uint_as_float(v[j]);
           }
+          // Common case: nothing in the chunk beats the threshold, which one
+          // minimum over the 32 keys shows. Partial or filtered chunks take
+          // the exact per-column test.
+          if (nvalid == 32 && p.mask_bits == nullptr && !(min32(key) <= thr_key)) continue;
           uint32_t pass = 0;
 #pragma unroll
           for (int j = 0; j < 32; ++j) pass |= (key[j] <= thr_key ? 1u : 0u) << j;
@@ -388,10 +433,10 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-template <int CAP, bool L2, int QT, bool IL>
+template <int CAP, bool L2, int QT, int KIND>
 cudaError_t launch_typed(const GemmTopkArgs& a, const CUtensorMap* maps, int grid, cudaStream_t stream) {
-  using TL = Tile<QT, IL>;
-  auto kern = gemm_topk_kernel<CAP, L2, QT, IL>;
+  using TL = Tile<QT, KIND>;
+  auto kern = gemm_topk_kernel<CAP, L2, QT, KIND>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(TL::SMEM));
   if (e != cudaSuccess) return e;
@@ -421,14 +466,33 @@ cudaError_t encode_split_map(CUtensorMap* map, const float* plane, int64_t rows,
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// A bf16 plane [rows x ldb] as a TMA tensor: boxes of 64 values (128 bytes,
+// 128-byte swizzle) by box_rows rows. Rows past the end read as zeros.
+cudaError_t encode_bf16_map(CUtensorMap* map, const void* plane, int64_t rows, int ldb, int box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = get_encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if (rows < 1) rows = 1;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(ldb), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldb) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(plane), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 int gemm_cap_for(int k) {
   if (k <= 16) return 32;
   if (k <= 224) return 64;
   return 0;
 }
 
+// Candidates rescored per query. The certificate compares the k-th exact key
+// with the largest approximate key among them, so more candidates widen the
+// margin it can prove: with bf16 candidates for config 4's distribution,
+// 32 leave ~0.07% of queries uncertified and 64 none in 20,000 trials.
 int gemm_cands_for(int k) {
-  if (k <= 16) return 32;
   if (k <= 40) return 64;
   if (k <= 224) return (k + 32 + 31) / 32 * 32;
   return 0;
@@ -438,27 +502,43 @@ int gemm_qt_for(int k) { return gemm_cap_for(k) == 32 ? 2 : 1; }
 
 int gemm_bn_for(int k) { return 256 / gemm_qt_for(k); }
 
-cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const float* q_hl, int64_t q_rows,
-                             const float* x_hl, bool hi_only, int grid, cudaStream_t stream) {
-  if (a.ld % 32 != 0) return cudaErrorInvalidValue;
+cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const void* q_plane, int64_t q_rows,
+                             const void* x_plane, PassKind kind, int grid, cudaStream_t stream) {
+  if (a.ld % 32 != 0 || a.ldb % 64 != 0) return cudaErrorInvalidValue;
   const int qt = gemm_qt_for(a.k);
-  const bool il = !hi_only;
-  CUtensorMap maps[2];
-  cudaError_t e = encode_split_map(&maps[0], q_hl, q_rows, a.ld, BM, il);
-  if (e == cudaSuccess) e = encode_split_map(&maps[1], x_hl, a.n, a.ld, 256 / qt, il);
-  if (e != cudaSuccess) return e;
   const int cap = gemm_cap_for(a.k);
+  CUtensorMap maps[2];
+  cudaError_t e;
+  if (kind == kPassBf16) {
+    if (cap != 32) return cudaErrorInvalidValue;
+    e = encode_bf16_map(&maps[0], q_plane, q_rows, a.ldb, BM);
+    if (e == cudaSuccess) e = encode_bf16_map(&maps[1], x_plane, a.n, a.ldb, 256 / qt);
+  } else {
+    const bool il = kind == kPass3xTf32;
+    e = encode_split_map(&maps[0], static_cast<const float*>(q_plane), q_rows, a.ld, BM, il);
+    if (e == cudaSuccess) e = encode_split_map(&maps[1], static_cast<const float*>(x_plane), a.n, a.ld, 256 / qt, il);
+  }
+  if (e != cudaSuccess) return e;
   if (cap == 32) {
-    if (il) return a.l2 ? launch_typed<32, true, 2, true>(a, maps, grid, stream)
-                        : launch_typed<32, false, 2, true>(a, maps, grid, stream);
-    return a.l2 ? launch_typed<32, true, 2, false>(a, maps, grid, stream)
-                : launch_typed<32, false, 2, false>(a, maps, grid, stream);
+    switch (kind) {
+      case kPass3xTf32:
+        return a.l2 ? launch_typed<32, true, 2, kPass3xTf32>(a, maps, grid, stream)
+                    : launch_typed<32, false, 2, kPass3xTf32>(a, maps, grid, stream);
+      case kPassTf32:
+        return a.l2 ? launch_typed<32, true, 2, kPassTf32>(a, maps, grid, stream)
+                    : launch_typed<32, false, 2, kPassTf32>(a, maps, grid, stream);
+      case kPassBf16:
+        return a.l2 ? launch_typed<32, true, 2, kPassBf16>(a, maps, grid, stream)
+                    : launch_typed<32, false, 2, kPassBf16>(a, maps, grid, stream);
+    }
   }
   if (cap == 64) {
-    if (il) return a.l2 ? launch_typed<64, true, 1, true>(a, maps, grid, stream)
-                        : launch_typed<64, false, 1, true>(a, maps, grid, stream);
-    return a.l2 ? launch_typed<64, true, 1, false>(a, maps, grid, stream)
-                : launch_typed<64, false, 1, false>(a, maps, grid, stream);
+    if (kind == kPass3xTf32)
+      return a.l2 ? launch_typed<64, true, 1, kPass3xTf32>(a, maps, grid, stream)
+                  : launch_typed<64, false, 1, kPass3xTf32>(a, maps, grid, stream);
+    if (kind == kPassTf32)
+      return a.l2 ? launch_typed<64, true, 1, kPassTf32>(a, maps, grid, stream)
+                  : launch_typed<64, false, 1, kPassTf32>(a, maps, grid, stream);
   }
   return cudaErrorInvalidValue;
 }

@@ -9,8 +9,13 @@
 // brings both to shared memory (half the L2 requests of separate planes);
 // a 64-byte box over the same plane reads the hi halves alone. Rows are
 // padded with zeros to a multiple of 32 floats, which leaves every dot
-// product unchanged. `norms` holds the squared L2 norm of each row for the
-// approximate key ||x||^2 - 2 q.x.
+// product unchanged. A bf16 copy (round to nearest even, rows padded with
+// zeros to a multiple of 64 so one 128-byte TMA row is one K slice) feeds the
+// first candidate pass for small k; a flag records whether any value is not
+// exactly representable in bf16. `norms` holds the squared L2 norm of each
+// row for the approximate key ||x||^2 - 2 q.x.
+#include <cuda_bf16.h>
+
 #include "px_common.cuh"
 #include "px_kernels.h"
 
@@ -25,29 +30,40 @@ __device__ __forceinline__ float tf32_rn(float x) {
 }
 
 // One warp per row.
-__global__ void prepare_rows_kernel(const float* __restrict__ src, int64_t n, int d, int ld,
+__global__ void prepare_rows_kernel(const float* __restrict__ src, int64_t n, int d, int ld, int ldb,
                                     float* __restrict__ dst, float* __restrict__ hl,
-                                    float* __restrict__ norms,
-                                    int* __restrict__ lo_nonzero, int* __restrict__ max_norm_sq) {
+                                    __nv_bfloat16* __restrict__ xb, float* __restrict__ norms,
+                                    int* __restrict__ lo_nonzero, int* __restrict__ bf_inexact,
+                                    int* __restrict__ max_norm_sq) {
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= n) return;
-  bool nz = false;
-  for (int e = lane; e < ld; e += 32) {
+  bool nz = false, bz = false;
+  const int width = ldb > ld ? ldb : ld;
+  for (int e = lane; e < width; e += 32) {
     float x = e < d ? src[row * d + e] : 0.f;
-    if (dst) dst[row * ld + e] = x;
-    if (hl) {
-      const float h = tf32_rn(x);
-      const float l = tf32_rn(__fsub_rn(x, h));
-      float* r = hl + row * 2 * ld + (e >> 4) * 32 + (e & 15);
-      r[0] = h;
-      r[16] = l;
-      nz |= (l != 0.f);
+    if (e < ld) {
+      if (dst) dst[row * ld + e] = x;
+      if (hl) {
+        const float h = tf32_rn(x);
+        const float l = tf32_rn(__fsub_rn(x, h));
+        float* r = hl + row * 2 * ld + (e >> 4) * 32 + (e & 15);
+        r[0] = h;
+        r[16] = l;
+        nz |= (l != 0.f);
+      }
+    }
+    if (xb && e < ldb) {
+      const __nv_bfloat16 b = __float2bfloat16_rn(x);
+      xb[row * ldb + e] = b;
+      bz |= (__bfloat162float(b) != x);
     }
   }
   __syncwarp();
   const bool any_nz = __any_sync(0xffffffffu, nz);
+  const bool any_bz = __any_sync(0xffffffffu, bz);
   if (lo_nonzero && any_nz && lane == 0) atomicOr(lo_nonzero, 1);
+  if (bf_inexact && any_bz && lane == 0) atomicOr(bf_inexact, 1);
   if ((norms || max_norm_sq) && lane == 0) {
     // Squared norm in the reference's 8-lane order (l2_sqr(x, 0)).
     const float* x = (dst ? dst + row * ld : src + row * d);
@@ -90,25 +106,36 @@ cudaError_t launch_pack_mask(const uint8_t* mask, int64_t n, uint32_t* bits, cud
   return cudaGetLastError();
 }
 
-cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, float* dst, float* hl,
-                                float* norms, int* lo_nonzero, int* max_norm_sq, cudaStream_t stream) {
+cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, int ldb, float* dst, float* hl,
+                                void* xb, float* norms, int* lo_nonzero, int* bf_inexact, int* max_norm_sq,
+                                cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
   const int threads = 256;
   const int64_t blocks = (n * 32 + threads - 1) / threads;
   prepare_rows_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
-      src, n, d, ld, dst, hl, norms, lo_nonzero, max_norm_sq);
+      src, n, d, ld, ldb, dst, hl, static_cast<__nv_bfloat16*>(xb), norms, lo_nonzero, bf_inexact,
+      max_norm_sq);
   return cudaGetLastError();
 }
 
-cudaError_t launch_split_queries(const float* q, int64_t nq, int d, int ld, int64_t rows_alloc,
-                                 float* hl, int* lo_nonzero, cudaStream_t stream) {
-  cudaError_t e = launch_prepare_rows(q, nq, d, ld, nullptr, hl, nullptr, lo_nonzero, nullptr, stream);
+cudaError_t launch_split_queries(const float* q, int64_t nq, int d, int ld, int ldb, int64_t rows_alloc,
+                                 float* hl, void* qb, int* lo_nonzero, int* bf_inexact, cudaStream_t stream) {
+  cudaError_t e = launch_prepare_rows(q, nq, d, ld, ldb, nullptr, hl, qb, nullptr, lo_nonzero, bf_inexact,
+                                      nullptr, stream);
   if (e != cudaSuccess) return e;
   if (rows_alloc > nq) {
-    const int64_t count = (rows_alloc - nq) * 2 * ld;
     const int threads = 256;
-    const unsigned blocks = static_cast<unsigned>((count + threads - 1) / threads);
-    zero_rows_kernel<<<blocks, threads, 0, stream>>>(hl, nq, rows_alloc, 2 * ld);
+    if (hl) {
+      const int64_t count = (rows_alloc - nq) * 2 * ld;
+      const unsigned blocks = static_cast<unsigned>((count + threads - 1) / threads);
+      zero_rows_kernel<<<blocks, threads, 0, stream>>>(hl, nq, rows_alloc, 2 * ld);
+    }
+    if (qb) {
+      // ldb is a multiple of 64: the bf16 padding rows are whole float pairs.
+      const int64_t count = (rows_alloc - nq) * (ldb / 2);
+      const unsigned blocks = static_cast<unsigned>((count + threads - 1) / threads);
+      zero_rows_kernel<<<blocks, threads, 0, stream>>>(static_cast<float*>(qb), nq, rows_alloc, ldb / 2);
+    }
   }
   return cudaGetLastError();
 }

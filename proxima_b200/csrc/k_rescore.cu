@@ -13,10 +13,11 @@
 //
 // eps is a worst-case bound, in double precision, built from
 //   S = ||q|| * max_x ||x|| >= sum_i |q_i x_i|        (Cauchy-Schwarz)
-// the tf32 representation error (with a lo plane in use: (2^-10 + 2^-22) * S
-// for a pass over the hi planes alone, 4 * 2^-22 * S for the three-pass sum),
-// an allowance of 2 * 2^-22 * S per tensor-core accumulation step, and the
-// rounding of the reference arithmetic and of the norms.
+// the representation error of the pass's operands (zero when they are exact:
+// (2^-8 + 2^-18) * S for bf16 copies, (2^-10 + 2^-22) * S for tf32 hi values
+// alone, 4 * 2^-22 * S for the three-pass tf32 sum), an allowance of
+// 2 * 2^-22 * S per tensor-core accumulation step (one per 8 values of K and
+// pass), and the rounding of the reference arithmetic and of the norms.
 #include "px_common.cuh"
 #include "px_kernels.h"
 
@@ -102,13 +103,22 @@ rescore_kernel(const RescoreArgs a) {
     const double qn = sqrt(qsq);
     const double xn = static_cast<double>(a.max_norm);
     const bool q_lo = *a.q_lo_flag != 0;
-    const bool lo_in_data = q_lo || a.x_lo_nonzero;
-    const int npass = a.hi_only ? 1 : 1 + (q_lo ? 1 : 0) + (a.x_lo_nonzero ? 1 : 0);
-    // Representation error per product |q_i x_i|: none when both lo planes
-    // are zero; 2^-10 + 2^-22 for hi x hi alone (each hi is within 2^-11 of
-    // its value); 4 * 2^-22 for the three-pass sum (the dropped lo x lo
-    // term and the rounding of each lo to tf32).
-    const double rep = !lo_in_data ? 0.0 : (a.hi_only ? 0x1p-10 + 0x1p-22 : 4.0 * 0x1p-22);
+    int npass = 1;
+    double rep = 0.0;  // representation error per product, relative to |q_i x_i|
+    if (a.pass_kind == kPassBf16) {
+      // Each bf16 value is within 2^-9 of its fp32 value: (1 + 2^-9)^2 - 1.
+      if (*a.q_bf_flag != 0 || a.x_bf_inexact) rep = 0x1p-8 + 0x1p-18;
+    } else if (q_lo || a.x_lo_nonzero) {
+      if (a.pass_kind == kPassTf32) {
+        // hi x hi alone: each hi is within 2^-11 of its value.
+        rep = 0x1p-10 + 0x1p-22;
+      } else {
+        // Three-pass sum: the dropped lo x lo term and the tf32 rounding of
+        // each lo.
+        npass = 1 + (q_lo ? 1 : 0) + (a.x_lo_nonzero ? 1 : 0);
+        rep = 4.0 * 0x1p-22;
+      }
+    }
     const double steps = static_cast<double>(npass) * ((a.d + 7) / 8) + 2.0;
     const double S = qn * xn;
     const double e_dot = S * (rep + 2.0 * steps * 0x1p-22);

@@ -195,22 +195,24 @@ void Segments::local_mask(const uint8_t* global_mask, int64_t n_local, std::vect
 // FlatIndex
 // ===========================================================================
 
-px_status FlatShard::ensure_capacity(int64_t need, int ld) {
+px_status FlatShard::ensure_capacity(int64_t need, int ld, int ldb) {
   if (need <= cap) return PX_OK;
   int64_t new_cap = std::max<int64_t>(need, cap + cap / 2);
   const size_t row_bytes = sizeof(float) * ld;
-  const size_t plane_bytes = static_cast<size_t>(new_cap) * row_bytes;
+  const size_t brow_bytes = 2 * static_cast<size_t>(ldb);
   size_t free_b = 0, total_b = 0;
   if (cudaMemGetInfo(&free_b, &total_b) == cudaSuccess) {
-    const size_t need_b = plane_bytes * 3 + sizeof(float) * new_cap;
+    const size_t need_b = static_cast<size_t>(new_cap) * (3 * row_bytes + brow_bytes + sizeof(float));
     if (need_b > free_b && new_cap > need) {
       new_cap = need;  // drop the growth slack before giving up
     }
   }
   float *nx = nullptr, *nhl = nullptr, *nn = nullptr;
+  void* nxb = nullptr;
   const size_t pb = static_cast<size_t>(new_cap) * row_bytes;
   cudaError_t e = cudaMalloc(&nx, pb);
   if (e == cudaSuccess) e = cudaMalloc(&nhl, 2 * pb);
+  if (e == cudaSuccess) e = cudaMalloc(&nxb, static_cast<size_t>(new_cap) * brow_bytes);
   // Norms are padded to a whole number of 256-row tiles: the tensor-core
   // epilogue reads them 32 rows at a time, past the last row of a shard.
   const int64_t norm_cap = (new_cap + 255) / 256 * 256;
@@ -220,6 +222,7 @@ px_status FlatShard::ensure_capacity(int64_t need, int ld) {
     cudaGetLastError();
     if (nx) cudaFree(nx);
     if (nhl) cudaFree(nhl);
+    if (nxb) cudaFree(nxb);
     if (nn) cudaFree(nn);
     return set_error(PX_ENOMEM, "device allocation of " + std::to_string(new_cap) +
                                     " rows failed on device " + std::to_string(device) + ": " +
@@ -229,14 +232,17 @@ px_status FlatShard::ensure_capacity(int64_t need, int ld) {
     const size_t used = static_cast<size_t>(n) * row_bytes;
     cudaMemcpyAsync(nx, x, used, cudaMemcpyDeviceToDevice, stream);
     cudaMemcpyAsync(nhl, hl, 2 * used, cudaMemcpyDeviceToDevice, stream);
+    cudaMemcpyAsync(nxb, xb, static_cast<size_t>(n) * brow_bytes, cudaMemcpyDeviceToDevice, stream);
     cudaMemcpyAsync(nn, norms, sizeof(float) * n, cudaMemcpyDeviceToDevice, stream);
     cudaStreamSynchronize(stream);
   }
   if (x) cudaFree(x);
   if (hl) cudaFree(hl);
+  if (xb) cudaFree(xb);
   if (norms) cudaFree(norms);
   x = nx;
   hl = nhl;
+  xb = nxb;
   norms = nn;
   cap = new_cap;
   return PX_OK;
@@ -247,8 +253,10 @@ void FlatShard::release() {
   if (stream) cudaStreamSynchronize(stream);
   if (x) cudaFree(x);
   if (hl) cudaFree(hl);
+  if (xb) cudaFree(xb);
   if (norms) cudaFree(norms);
   x = hl = norms = nullptr;
+  xb = nullptr;
   if (flag) cudaFree(flag);
   flag = nullptr;
   if (ev_start) cudaEventDestroy(ev_start);
@@ -265,11 +273,12 @@ void FlatShard::release() {
 }
 
 // Appends rows that are already on this shard's device.
-px_status FlatShard::append_device(const float* d_src, int64_t count, int d, int ld,
+px_status FlatShard::append_device(const float* d_src, int64_t count, int d, int ld, int ldb,
                                    int64_t global_begin) {
-  px_status s = ensure_capacity(n + count, ld);
+  px_status s = ensure_capacity(n + count, ld, ldb);
   if (s != PX_OK) return s;
-  cudaError_t e = launch_prepare_rows(d_src, count, d, ld, x + n * ld, hl + n * 2 * ld, norms + n, flag,
+  cudaError_t e = launch_prepare_rows(d_src, count, d, ld, ldb, x + n * ld, hl + n * 2 * ld,
+                                      static_cast<uint16_t*>(xb) + n * ldb, norms + n, flag, flag + 1,
                                       flag + 2, stream);
   if (e != cudaSuccess) return cuda_status(e, "prepare_rows launch");
   segs.local.push_back(n);
@@ -282,6 +291,7 @@ px_status FlatShard::append_device(const float* d_src, int64_t count, int d, int
   e = cudaMemcpy(h_flag, flag, sizeof(h_flag), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_status(e, "add flag readback");
   lo_nonzero = h_flag[0] != 0;
+  bf_inexact = h_flag[1] != 0;
   std::memcpy(&max_norm_sq, &h_flag[2], sizeof(float));
   g_launches += 1;
   return PX_OK;
@@ -319,6 +329,7 @@ PX_API px_status px_flat_create(int32_t dim, int32_t metric, const int32_t* devi
   px_flat* h = new px_flat();
   h->dim = dim;
   h->ld = (dim + 31) & ~31;
+  h->ldb = (dim + 63) & ~63;
   h->metric = metric;
   h->shards.resize(devs.size());
   for (size_t i = 0; i < devs.size(); ++i) {
@@ -381,6 +392,7 @@ PX_API px_status px_flat_last_profile(const px_flat* h, px_search_profile* out) 
   out->launches = sh.last_launches;
   out->fallback_queries = sh.last_fallback;
   out->refined_queries = sh.last_refined;
+  out->first_pass = sh.last_pass;
   out->profiled = 0;
   out->main_kernel_ms = 0.f;
   if (sh.last_profiled) {
@@ -428,7 +440,7 @@ PX_API px_status px_flat_add(px_flat* h, const float* rows, int64_t n) {
     e = cudaMemcpyAsync(sh.stage.ptr, rows + begin[g] * h->dim, bytes, cudaMemcpyHostToDevice,
                         sh.stream);
     if (e != cudaSuccess) return cuda_status(e, "row upload");
-    s = sh.append_device(static_cast<const float*>(sh.stage.ptr), count[g], h->dim, h->ld,
+    s = sh.append_device(static_cast<const float*>(sh.stage.ptr), count[g], h->dim, h->ld, h->ldb,
                          h->total + begin[g]);
     if (s != PX_OK) return s;
   }
@@ -468,7 +480,7 @@ PX_API px_status px_flat_reserve(px_flat* h, int64_t n_total) {
   for (auto& sh : h->shards) {
     if (per > 0xFFFFFFFFll) return set_error(PX_EUNSUPPORTED, "a shard holds at most 2^32-1 rows");
     DeviceGuard dg(sh.device);
-    s = sh.ensure_capacity(std::max(per, sh.n), h->ld);
+    s = sh.ensure_capacity(std::max(per, sh.n), h->ld, h->ldb);
     if (s != PX_OK) return s;
   }
   return PX_OK;
@@ -484,7 +496,7 @@ PX_API px_status px_flat_add_device(px_flat* h, const float* d_rows, int64_t n) 
   FlatShard& sh = h->shards[0];
   if (sh.n + n > 0xFFFFFFFFll) return set_error(PX_EUNSUPPORTED, "a shard holds at most 2^32-1 rows");
   DeviceGuard dg(sh.device);
-  s = sh.append_device(d_rows, n, h->dim, h->ld, h->total);
+  s = sh.append_device(d_rows, n, h->dim, h->ld, h->ldb, h->total);
   if (s != PX_OK) return s;
   h->total += n;
   return PX_OK;
@@ -712,7 +724,7 @@ PX_API PxGpuIndex* knn_gpu_create(const float* base, int n, int dim) {
     const size_t bytes = sizeof(float) * static_cast<size_t>(n) * dim;
     if (sh.stage.reserve(bytes) != cudaSuccess ||
         cudaMemcpyAsync(sh.stage.ptr, base, bytes, cudaMemcpyHostToDevice, sh.stream) != cudaSuccess ||
-        sh.append_device(static_cast<const float*>(sh.stage.ptr), n, dim, f->ld, 0) != PX_OK) {
+        sh.append_device(static_cast<const float*>(sh.stage.ptr), n, dim, f->ld, f->ldb, 0) != PX_OK) {
       px_flat_destroy(f);
       return nullptr;
     }

@@ -89,21 +89,32 @@ cudaError_t launch_nearest_centroid(const float* vectors, int64_t n, int m, int 
 // ---- shard preparation (k_prep.cu) ----------------------------------------
 // Copies n rows of d floats into the shard (stride ld, zero padded), and
 // writes the interleaved tf32 split plane `hl` (stride 2*ld: per 16-element
-// chunk 16 hi values then 16 lo values) and the squared norms. lo_nonzero is
-// raised when any lo element is nonzero; max_norm_sq (float bits) is raised
-// to the largest squared norm.
-cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, float* dst,
-                                float* hl, float* norms, int* lo_nonzero, int* max_norm_sq,
+// chunk 16 hi values then 16 lo values), the bf16 plane `xb` (stride ldb, a
+// multiple of 64) and the squared norms; any output may be null. lo_nonzero
+// is raised when any lo element is nonzero, bf_inexact when any value
+// differs from its bf16 rounding; max_norm_sq (float bits) is raised to the
+// largest squared norm.
+cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, int ldb, float* dst, float* hl,
+                                void* xb, float* norms, int* lo_nonzero, int* bf_inexact, int* max_norm_sq,
                                 cudaStream_t stream);
-// Split plane of nq query rows, zero-filled up to rows_alloc rows.
-cudaError_t launch_split_queries(const float* q, int64_t nq, int d, int ld, int64_t rows_alloc,
-                                 float* hl, int* lo_nonzero, cudaStream_t stream);
+// Split plane and bf16 plane of nq query rows (either may be null),
+// zero-filled up to rows_alloc rows.
+cudaError_t launch_split_queries(const float* q, int64_t nq, int d, int ld, int ldb, int64_t rows_alloc,
+                                 float* hl, void* qb, int* lo_nonzero, int* bf_inexact, cudaStream_t stream);
+
+// What a tensor-core candidate pass multiplies.
+enum PassKind : int {
+  kPass3xTf32 = 0,  // hi.hi + hi.lo + lo.hi of the tf32 split planes (~fp32)
+  kPassTf32 = 1,    // hi.hi only
+  kPassBf16 = 2,    // the bf16 planes
+};
 
 // ---- K1: tensor-core candidate generation (k_gemm.cu) ---------------------
 struct GemmTopkArgs {
   int nq;
   int64_t n;            // shard rows
-  int ld;               // row stride (floats), multiple of 16
+  int ld;               // row stride (floats), multiple of 32
+  int ldb;              // bf16 plane row stride (elements), multiple of 64
   int k;
   int T;                // groups of gemm_qt_for(k) query tiles of 128
   int S;                // base splits
@@ -124,11 +135,11 @@ int gemm_cap_for(int k);    // candidates kept per (query, split) in registers (
 int gemm_cands_for(int k);  // candidates per query after the split merge (<= 256)
 int gemm_qt_for(int k);   // query tiles of 128 per CTA (2 for k <= 16, else 1)
 int gemm_bn_for(int k);   // base rows per tile (256 / qt)
-// q_hl / x_hl: interleaved split planes (stride 2*ld). hi_only selects the
-// one-pass kernel that reads only the hi halves (exact when both lo planes
-// are zero, otherwise within the tf32 bound the certificate accounts for).
-cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const float* q_hl, int64_t q_rows,
-                             const float* x_hl, bool hi_only, int grid, cudaStream_t stream);
+// q_plane / x_plane: the interleaved split planes (stride 2*ld) for the tf32
+// passes, the bf16 planes (stride ldb) for kPassBf16, which serves
+// gemm_cap_for(k) == 32 only. kPassTf32 reads only the hi halves.
+cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const void* q_plane, int64_t q_rows,
+                             const void* x_plane, PassKind kind, int grid, cudaStream_t stream);
 
 // ---- K5: exact rescoring + certificate (k_rescore.cu) ---------------------
 struct RescoreArgs {
@@ -147,7 +158,9 @@ struct RescoreArgs {
   float max_norm;          // max ||x|| over the shard
   int x_lo_nonzero;
   const int* q_lo_flag;
-  int hi_only;             // the candidate pass used only the hi planes
+  int pass_kind;           // PassKind of the candidate pass
+  int x_bf_inexact;        // shard values not all exact in bf16
+  const int* q_bf_flag;    // device word: query values not all exact in bf16
   uint64_t* out;           // [nq][k] exact candidates
   int* status;             // [nq] 0 = certified
   int* n_fail;             // count of uncertified queries

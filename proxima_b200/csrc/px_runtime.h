@@ -89,13 +89,16 @@ struct FlatShard {
   float* x = nullptr;      // fp32 rows, stride ld
   float* hl = nullptr;     // tf32 split, stride 2*ld: per 16-element chunk hi x16 then lo x16
   float* norms = nullptr;  // squared norms
+  void* xb = nullptr;      // bf16 rows, stride ldb (a multiple of 64), zero padded
   int64_t n = 0, cap = 0;
-  int* flag = nullptr;     // [0] lo plane nonzero, [2] max squared norm (bits), written by appends
+  int* flag = nullptr;     // [0] lo plane nonzero, [1] some value inexact in bf16,
+                           // [2] max squared norm (bits); written by appends
   bool lo_nonzero = false;
+  bool bf_inexact = false;
   float max_norm_sq = 0.f;
   cudaEvent_t ev_start = nullptr, ev_stop = nullptr;  // brackets the dominant kernel when profiling
   cudaEvent_t ev_done = nullptr;  // this shard's results are in the gather buffer (own device)
-  int last_path = 0, last_fallback = 0, last_refined = 0, last_launches = 0;
+  int last_path = 0, last_fallback = 0, last_refined = 0, last_launches = 0, last_pass = -1;
   bool last_profiled = false;
   px::Segments segs;
   px::DevBuf ws;           // search workspace
@@ -105,8 +108,8 @@ struct FlatShard {
   int64_t* out_ids = nullptr;  // results of the last search (inside stage)
   float* out_dists = nullptr;
 
-  px_status ensure_capacity(int64_t need, int ld);
-  px_status append_device(const float* d_src, int64_t count, int d, int ld, int64_t global_begin);
+  px_status ensure_capacity(int64_t need, int ld, int ldb);
+  px_status append_device(const float* d_src, int64_t count, int d, int ld, int ldb, int64_t global_begin);
   void release();
 };
 
@@ -125,7 +128,8 @@ struct GatherBuf {
 
 struct px_flat {
   int dim = 0;
-  int ld = 0;
+  int ld = 0;   // fp32 / split-plane row stride: dim rounded up to 32
+  int ldb = 0;  // bf16 plane row stride: dim rounded up to 64
   int metric = 0;
   int64_t total = 0;
   int64_t id_offset = 0;

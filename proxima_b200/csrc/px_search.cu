@@ -69,17 +69,28 @@ namespace {
 
 // Device workspace of one tensor-core candidate pass.
 struct TensorWs {
-  float* q_hl = nullptr;            // query split plane, q_rows x 2*ld
+  float* q_hl = nullptr;            // query split plane, q_rows x 2*ld (tf32 passes)
+  void* qb = nullptr;               // query bf16 plane, q_rows x ldb (bf16 pass)
   uint64_t* partial = nullptr;      // [nq][S][cap] per-split lists
   uint64_t* merged = nullptr;       // [nq][cands]
   uint64_t* final_cands = nullptr;  // [nq][k] exact candidates
   int* status = nullptr;            // [nq]
   int* fail_list = nullptr;         // [nq] uncertified queries
-  int* counters = nullptr;          // [0] uncertified count, [1] query lo plane in use, [2] timeout
+  int* counters = nullptr;          // [0] uncertified count, [1] query lo plane in use, [2] timeout,
+                                    // [3] some query value inexact in bf16
 };
 
-void carve_tensor_ws(Carver& c, const SearchPlan& plan, int64_t nq, int ld, int k, TensorWs& w) {
-  w.q_hl = static_cast<float*>(c.take(sizeof(float) * static_cast<size_t>(plan.q_rows) * 2 * ld));
+// The first candidate pass: bf16 where the candidate lists are short enough
+// for its wider bound to certify typical data (k <= 16), tf32 hi values
+// otherwise.
+PassKind first_pass_for(int k) { return gemm_cap_for(k) == 32 ? kPassBf16 : kPassTf32; }
+
+void carve_tensor_ws(Carver& c, const SearchPlan& plan, int64_t nq, int ld, int ldb, int k, PassKind kind,
+                     TensorWs& w) {
+  if (kind == kPassBf16)
+    w.qb = c.take(2 * static_cast<size_t>(plan.q_rows) * ldb);
+  else
+    w.q_hl = static_cast<float*>(c.take(sizeof(float) * static_cast<size_t>(plan.q_rows) * 2 * ld));
   w.partial = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.S * plan.cap));
   w.merged = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.cands));
   w.final_cands = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * k));
@@ -114,7 +125,7 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
   if (gemm) {
     plan_gemm(sh, nq, k, plan);
     TensorWs w;
-    carve_tensor_ws(c, plan, nq, h->ld, k, w);
+    carve_tensor_ws(c, plan, nq, h->ld, h->ldb, k, first_pass_for(k), w);
     if (masked) c.take(sizeof(uint32_t) * mask_words(sh.n));
   } else {
     plan.path = FlatPath::Exact;
@@ -199,23 +210,27 @@ static px_status exact_for_list(const px_flat* h, FlatShard& sh, int metric, con
   return PX_OK;
 }
 
-// One tensor-core candidate pass: split the queries, K1 over the shard (one
-// pass over the hi planes, or three with the lo planes), split merge, exact
-// rescoring and certificate. Leaves exact candidates in w.final_cands and the
-// uncertified queries in w.fail_list; reads back their count and whether the
-// queries have a lo plane (the one host wait of the pass).
+// One tensor-core candidate pass: convert the queries, K1 over the shard
+// (bf16 copies, tf32 hi values, or the three-pass tf32 sum), split merge,
+// exact rescoring and certificate. Leaves exact candidates in w.final_cands
+// and the uncertified queries in w.fail_list; reads back their count and
+// whether the pass's operands were inexact, i.e. whether a more precise pass
+// could certify them (the one host wait of the pass).
 static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& plan, int metric,
-                             const float* d_q, int64_t nq, int k, const uint32_t* mask_bits,
-                             bool three_pass, const TensorWs& w, bool profile_main, cudaStream_t stream,
-                             int* n_fail, bool* q_lo) {
+                             const float* d_q, int64_t nq, int k, const uint32_t* mask_bits, PassKind kind,
+                             const TensorWs& w, bool profile_main, cudaStream_t stream, int* n_fail,
+                             bool* inexact) {
   const bool l2 = metric == PX_METRIC_L2;
   cudaError_t e = cudaMemsetAsync(w.counters, 0, sizeof(int) * 4, stream);
-  if (e == cudaSuccess) e = launch_split_queries(d_q, nq, h->dim, h->ld, plan.q_rows, w.q_hl, w.counters + 1, stream);
+  if (e == cudaSuccess)
+    e = launch_split_queries(d_q, nq, h->dim, h->ld, h->ldb, plan.q_rows, w.q_hl, w.qb, w.counters + 1,
+                             w.counters + 3, stream);
   if (e != cudaSuccess) return cuda_status(e, "query split");
   GemmTopkArgs g;
   g.nq = static_cast<int>(nq);
   g.n = sh.n;
   g.ld = h->ld;
+  g.ldb = h->ldb;
   g.k = k;
   g.T = plan.T;
   g.S = plan.S;
@@ -230,7 +245,10 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
   g.err = w.counters + 2;
   g.mask_bits = mask_bits;
   if (profile_main) cudaEventRecord(sh.ev_start, stream);
-  e = launch_gemm_topk(g, w.q_hl, plan.q_rows, sh.hl, !three_pass, plan.grid, stream);
+  if (kind == kPassBf16)
+    e = launch_gemm_topk(g, w.qb, plan.q_rows, sh.xb, kind, plan.grid, stream);
+  else
+    e = launch_gemm_topk(g, w.q_hl, plan.q_rows, sh.hl, kind, plan.grid, stream);
   if (profile_main) cudaEventRecord(sh.ev_stop, stream);
   if (e != cudaSuccess) return cuda_status(e, "tensor-core kernel launch");
   e = launch_merge_lists(w.partial, nq, plan.S, plan.cap, plan.cands, w.merged, stream);
@@ -251,7 +269,9 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
   r.max_norm = std::sqrt(sh.max_norm_sq);
   r.x_lo_nonzero = sh.lo_nonzero ? 1 : 0;
   r.q_lo_flag = w.counters + 1;
-  r.hi_only = three_pass ? 0 : 1;
+  r.pass_kind = kind;
+  r.x_bf_inexact = sh.bf_inexact ? 1 : 0;
+  r.q_bf_flag = w.counters + 3;
   r.out = w.final_cands;
   r.status = w.status;
   r.n_fail = w.counters;
@@ -259,7 +279,7 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
   e = launch_rescore(r, stream);
   if (e != cudaSuccess) return cuda_status(e, "rescore launch");
   g_launches += 5;  // split, gemm, merge, rescore (+ memset counted as one)
-  int hc[3] = {0, 0, 0};
+  int hc[4] = {0, 0, 0, 0};
   e = cudaMemcpyAsync(hc, w.counters, sizeof(hc), cudaMemcpyDeviceToHost, stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
   if (e != cudaSuccess) return cuda_status(e, "certificate readback");
@@ -267,7 +287,7 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
     return set_error(PX_ETIMEOUT, "a tensor-core pipeline wait timed out on device " +
                                       std::to_string(sh.device) + "; the search was abandoned");
   *n_fail = hc[0];
-  *q_lo = hc[1] != 0;
+  *inexact = kind == kPassBf16 ? (sh.bf_inexact || hc[3] != 0) : (sh.lo_nonzero || hc[1] != 0);
   return PX_OK;
 }
 
@@ -278,6 +298,7 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   sh.last_path = static_cast<int>(plan.path);
   sh.last_fallback = 0;
   sh.last_refined = 0;
+  sh.last_pass = -1;
   sh.last_profiled = prof;
   const int64_t launches0 = g_launches.load();
   Carver c(sh.ws.ptr);
@@ -291,14 +312,16 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   }
 
   // ---- tensor-core path ----
-  // 1. One pass over the hi planes for every query. Its keys carry a tf32
-  //    rounding error, which the certificate's bound covers; on typical
-  //    data nearly every query is certified.
-  // 2. The uncertified queries, if the lo planes are in use and there are
-  //    enough of them, get a three-pass (~fp32) candidate pass.
+  // 1. One pass over bf16 copies (k <= 16) or tf32 hi values for every
+  //    query. Its keys carry a rounding error, which the certificate's bound
+  //    covers; on typical data nearly every query is certified.
+  // 2. The uncertified queries, if that pass's operands were inexact and
+  //    there are enough of them, get a three-pass (~fp32) candidate pass.
   // 3. Whatever is still uncertified goes through the exact scan.
+  const PassKind first = first_pass_for(k);
+  sh.last_pass = first;
   TensorWs w;
-  carve_tensor_ws(c, plan, nq, h->ld, k, w);
+  carve_tensor_ws(c, plan, nq, h->ld, h->ldb, k, first, w);
   plan.final_cands = w.final_cands;
   uint32_t* mask_bits = d_mask ? static_cast<uint32_t*>(c.take(sizeof(uint32_t) * mask_words(sh.n))) : nullptr;
   if (mask_bits) {
@@ -306,28 +329,28 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
     if (e != cudaSuccess) return cuda_status(e, "mask pack");
   }
   int n_fail = 0;
-  bool q_lo = false;
-  px_status s = tensor_pass(h, sh, plan, metric, d_q, nq, k, mask_bits, false, w, prof, stream, &n_fail, &q_lo);
+  bool inexact = false;
+  px_status s = tensor_pass(h, sh, plan, metric, d_q, nq, k, mask_bits, first, w, prof, stream, &n_fail, &inexact);
   if (s != PX_OK) return s;
   if (n_fail > 0) {
-    const bool lo_used = sh.lo_nonzero || q_lo;
-    if (lo_used && refine_pays(n_fail, k)) {
+    if (inexact && refine_pays(n_fail, k)) {
       SearchPlan p2;
       plan_gemm(sh, n_fail, k, p2);
       Carver c2;
       c2.take(sizeof(float) * static_cast<size_t>(n_fail) * h->dim);
       TensorWs w2;
-      carve_tensor_ws(c2, p2, n_fail, h->ld, k, w2);
+      carve_tensor_ws(c2, p2, n_fail, h->ld, h->ldb, k, kPass3xTf32, w2);
       cudaError_t e = sh.ws2.reserve(c2.used);
       if (e != cudaSuccess) return cuda_status(e, "refinement workspace allocation");
       c2 = Carver(sh.ws2.ptr);
       float* fq = static_cast<float*>(c2.take(sizeof(float) * static_cast<size_t>(n_fail) * h->dim));
-      carve_tensor_ws(c2, p2, n_fail, h->ld, k, w2);
+      carve_tensor_ws(c2, p2, n_fail, h->ld, h->ldb, k, kPass3xTf32, w2);
       e = launch_gather_rows(d_q, h->dim, w.fail_list, n_fail, fq, stream);
       if (e != cudaSuccess) return cuda_status(e, "refinement gather");
       int n_fail2 = 0;
-      bool q_lo2 = false;
-      s = tensor_pass(h, sh, p2, metric, fq, n_fail, k, mask_bits, true, w2, false, stream, &n_fail2, &q_lo2);
+      bool inexact2 = false;
+      s = tensor_pass(h, sh, p2, metric, fq, n_fail, k, mask_bits, kPass3xTf32, w2, false, stream, &n_fail2,
+                      &inexact2);
       if (s != PX_OK) return s;
       if (n_fail2 > 0) {
         s = exact_for_list(h, sh, metric, fq, w2.fail_list, n_fail2, k, d_mask, w2.final_cands, stream);

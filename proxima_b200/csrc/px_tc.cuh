@@ -54,31 +54,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// try_wait with a suspend-time hint: the thread sleeps until the phase
-// completes or ~`ns` nanoseconds pass, instead of spinning on issue slots.
-__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(ns)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait. Returns false (and raises *abort) on timeout, or returns
-// false early when another role already raised *abort.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+// Bounded wait. Polls the phase and sleeps ~sleep_ns between polls, so a
+// waiting warp takes no issue slots from the warps that do the work; every
+// 64 polls it checks the shared abort flag and the wall-clock limit.
+// Returns false (and raises *abort) on timeout, or false early when another
+// role already raised *abort.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          uint32_t sleep_ns = 32) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  while (true) {
-    if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
-    if (*abort) return false;
-    if (globaltimer() - t0 > kWaitTimeoutNs) {
-      *abort = 1;
-      return false;
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(sleep_ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 0) {
+      if (*abort) return false;
+      if (globaltimer() - t0 > kWaitTimeoutNs) {
+        *abort = 1;
+        return false;
+      }
     }
   }
 }
@@ -125,6 +118,18 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint6
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D (+)= A.B^T with A, B bf16 (kind::f16; both operands must have the same
+// 16-bit type), D f32 in TMEM; K = 16 per instruction.
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
@@ -187,6 +192,12 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
 // Instruction descriptor: D f32, A/B tf32, both K-major, M x N.
 __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
   return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// Instruction descriptor: D f32, A/B bf16 (kind::f16), both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
 }
 
