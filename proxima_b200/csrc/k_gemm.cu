@@ -126,6 +126,69 @@ __device__ __forceinline__ void list_sort(uint64_t (&L)[CAP]) {
   }
 }
 
+// Drains NCOL accumulator columns (base rows row0 ..) of this thread's TMEM
+// lane into its top-CAP list: approximate keys, a three-input min tree that
+// rejects a 32-column chunk in the common case, and the exact per-column test
+// and insertion otherwise. taddr: the lane's TMEM address of column 0.
+template <int CAP, bool L2, int NCOL>
+__device__ __forceinline__ void drain_columns(uint64_t (&L)[CAP], uint64_t& thr, float& thr_key, int& maxpos,
+                                              uint32_t taddr, int64_t row0, int valid_cols,
+                                              const GemmTopkArgs& p, float* slot) {
+#pragma unroll 1
+  for (int c = 0; c < NCOL / 32; ++c) {
+    __syncwarp();  // the tcgen05.ld below is .sync.aligned
+    uint32_t v[32];
+    tc::tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), v);
+    tc::tmem_ld_wait();
+    const int64_t rbase = row0 + c * 32;
+    const int nvalid = valid_cols - c * 32;
+    if (nvalid <= 0) continue;
+    // Hot path: the approximate keys of 32 columns.
+    float key[32];
+    if (L2) {
+      const float4* nrm = reinterpret_cast<const float4*>(p.norms + rbase);
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 nv = __ldg(nrm + j4);
+        key[4 * j4 + 0] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 0]), nv.x);
+        key[4 * j4 + 1] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 1]), nv.y);
+        key[4 * j4 + 2] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 2]), nv.z);
+        key[4 * j4 + 3] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 3]), nv.w);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) key[j] = -__uint_as_float(v[j]);
+    }
+    // Common case: nothing in the chunk beats the threshold, which one
+    // minimum over the 32 keys shows. Partial or filtered chunks take
+    // the exact per-column test.
+    if (nvalid == 32 && p.mask_bits == nullptr && !(min32(key) <= thr_key)) continue;
+    uint32_t pass = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) pass |= (key[j] <= thr_key ? 1u : 0u) << j;
+    if (nvalid < 32) pass &= (1u << nvalid) - 1u;
+    if (p.mask_bits) pass &= __ldg(p.mask_bits + (rbase >> 5));  // rbase is a multiple of 32
+    if (pass) {
+      // Rare path, one copy of the insertion code: keys go through
+      // this thread's slot (shared or local memory) so they can be indexed.
+#pragma unroll
+      for (int j = 0; j < 32; ++j) slot[j] = key[j];
+      while (pass) {
+        const int j = __ffs(pass) - 1;
+        pass &= pass - 1;
+        const float kj = slot[j];
+        if (kj <= thr_key) {
+          const uint64_t cand = pack_cand(kj, static_cast<uint32_t>(rbase + j));
+          if (cand < thr) {
+            list_insert<CAP>(L, thr, maxpos, cand);
+            thr_key = thr == PX_EMPTY ? __int_as_float(0x7f800000) : cand_key(thr);
+          }
+        }
+      }
+    }
+  }
+}
+
 template <int CAP, bool L2, int QT, int KIND>
 __global__ void __launch_bounds__(Tile<QT, KIND>::THREADS, 1)
 gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_x,
@@ -341,59 +404,7 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         // Columns of this tile that are real rows (the last tile may be short).
         const int valid_cols = p.n - row0 < BN ? static_cast<int>(p.n - row0) : BN;
         const uint32_t col0 = static_cast<uint32_t>((acc * QT + wg) * BN);
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          __syncwarp();  // the tcgen05.ld below is .sync.aligned
-          uint32_t v[32];
-          tc::tmem_ld_32x32b_x32(lane_addr + col0 + static_cast<uint32_t>(c * 32), v);
-          tc::tmem_ld_wait();
-          const int64_t rbase = row0 + c * 32;
-          const int nvalid = valid_cols - c * 32;
-          if (nvalid <= 0) continue;
-          // Hot path: the approximate keys of 32 columns.
-          float key[32];
-          if (L2) {
-            const float4* nrm = reinterpret_cast<const float4*>(p.norms + rbase);
-#pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-              const float4 nv = __ldg(nrm + j4);
-              key[4 * j4 + 0] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 0]), nv.x);
-              key[4 * j4 + 1] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 1]), nv.y);
-              key[4 * j4 + 2] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 2]), nv.z);
-              key[4 * j4 + 3] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 3]), nv.w);
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) key[j] = -__uint_as_float(v[j]);
-          }
-          // Common case: nothing in the chunk beats the threshold, which one
-          // minimum over the 32 keys shows. Partial or filtered chunks take
-          // the exact per-column test.
-          if (nvalid == 32 && p.mask_bits == nullptr && !(min32(key) <= thr_key)) continue;
-          uint32_t pass = 0;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) pass |= (key[j] <= thr_key ? 1u : 0u) << j;
-          if (nvalid < 32) pass &= (1u << nvalid) - 1u;
-          if (p.mask_bits) pass &= __ldg(p.mask_bits + (rbase >> 5));  // rbase is a multiple of 32
-          if (pass) {
-            // Rare path, one copy of the insertion code: keys go through
-            // this thread's shared-memory slot so they can be indexed.
-#pragma unroll
-            for (int j = 0; j < 32; ++j) slot[j] = key[j];
-            while (pass) {
-              const int j = __ffs(pass) - 1;
-              pass &= pass - 1;
-              const float kj = slot[j];
-              if (kj <= thr_key) {
-                const uint64_t cand = pack_cand(kj, static_cast<uint32_t>(rbase + j));
-                if (cand < thr) {
-                  list_insert<CAP>(L, thr, maxpos, cand);
-                  thr_key = thr == PX_EMPTY ? __int_as_float(0x7f800000) : cand_key(thr);
-                }
-              }
-            }
-          }
-        }
+        drain_columns<CAP, L2, BN>(L, thr, thr_key, maxpos, lane_addr + col0, row0, valid_cols, p, slot);
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(tempty_bar(acc));
@@ -420,6 +431,265 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   if (threadIdx.x == 0 && *s_abort) atomicOr(p.err, 1);
 }
 
+// ---------------------------------------------------------------------------
+// The bf16 pass on CTA pairs (tcgen05 cta_group::2).
+//
+// A cluster of two CTAs computes 256 queries x 256 base rows per tile: each
+// CTA stages its 128 query rows and 128 of the base rows (K slices of 64 bf16
+// values, 128-byte swizzle), and the even CTA issues M = 256, N = 256 MMAs
+// that read both CTAs' shared memory and write each CTA's TMEM (its 128
+// queries x 256 columns). Per CTA that is 256 staged rows for 128 x 256
+// outputs, against 384 rows for 256 x 128 outputs in the single-CTA kernel:
+// 1.5x less operand traffic from L2 per output.
+//
+// Barriers (no multicast anywhere; the even CTA commits to each CTA's
+// barrier separately):
+//   full[s]   even CTA; armed by its producer for both CTAs' bytes, and both
+//             CTAs' TMA loads complete on it
+//   empty[s]  each CTA; stage s consumed by the MMAs
+//   tfull[a]  each CTA; accumulator a holds a finished tile
+//   tempty[a] even CTA; 16 arrivals, the 8 epilogue warps of each CTA
+//   done      each CTA; every MMA has completed
+// Each CTA's two epilogue warpgroups drain 128 columns each of every tile, so
+// every (query, split) has two lists. The epilogue's rare insertion path
+// indexes its keys through local memory, so shared memory holds only the
+// ring. (A seventh stage, or prefetching base slices into L2 ahead of the
+// ring, measured slower on config 4.)
+namespace pairk {
+constexpr int PM = 128;                         // query rows per CTA (TMEM lanes)
+constexpr int PH = 128;                         // base rows staged per CTA
+constexpr int ROW = 128;                        // bytes per row per stage: 64 bf16
+constexpr int STAGES = 6;
+constexpr int A_TILE = PM * ROW;                // 16 KB
+constexpr int STAGE_BYTES = A_TILE + PH * ROW;  // 32 KB
+constexpr int NBARS = 2 * STAGES + 2 + 2 + 1;
+constexpr int THREADS = 64 + 256;
+constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + NBARS * 8 + 16;
+}  // namespace pairk
+
+// Candidates kept per (query, split, column half) by the pair kernel. A list
+// over ~10^5 rows refills ~CAP * ln(rows / CAP) times at a cost linear in CAP,
+// while the merge needs only the best 64 per query across all lists (spread
+// ~1 per list): 16 keeps every k <= 16 certifiable even when one list holds
+// all the neighbours, at a quarter of the insertion work of 32.
+constexpr int kPairCap = 16;
+
+template <bool L2, int CAP>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairk::THREADS, 1)
+gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_x,
+                      const GemmTopkArgs p) {
+  using namespace pairk;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NBARS);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = tc::cluster_ctarank();
+  const bool leader = rank == 0;
+  const uint32_t smem_base = tc::smem_addr(smem);
+  auto full_bar = [&](int s) { return tc::smem_addr(&bars[s]); };
+  auto empty_bar = [&](int s) { return tc::smem_addr(&bars[STAGES + s]); };
+  auto tfull_bar = [&](int a) { return tc::smem_addr(&bars[2 * STAGES + a]); };
+  auto tempty_bar = [&](int a) { return tc::smem_addr(&bars[2 * STAGES + 2 + a]); };
+  const uint32_t done_bar = tc::smem_addr(&bars[2 * STAGES + 4]);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(full_bar(s), 1);
+      tc::mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(tfull_bar(a), 1);
+      tc::mbar_init(tempty_bar(a), 16);
+    }
+    tc::mbar_init(done_bar, 1);
+    *s_abort = 0;
+    tc::fence_mbarrier_init_cluster();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tmap(&tm_q);
+    tc::prefetch_tmap(&tm_x);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc_pair(tc::smem_addr(s_tmem), kTmemCols);
+    tc::tmem_relinquish_pair();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::cluster_sync();  // both CTAs' barriers are initialised before any use
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+  const int KC = p.ldb / 64;
+  const int cluster = static_cast<int>(tc::cluster_id_x());
+  const int nclusters = static_cast<int>(tc::nclusters_x());
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_phase[STAGES];
+      bool issued[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) {
+        issued[s] = false;
+        issued_phase[s] = 0;
+      }
+      bool ok = true;
+      for (int item = cluster; ok && item < p.n_items; item += nclusters) {
+        const int qg = item % p.T;
+        const int split = item / p.T;
+        const int t0 = split * p.tiles_per_split;
+        const int t1 = min(p.nb, t0 + p.tiles_per_split);
+        for (int t = t0; ok && t < t1; ++t) {
+          for (int kc = 0; kc < KC; ++kc) {
+            if (!tc::mbar_wait(empty_bar(stage), phase ^ 1, s_abort)) {
+              ok = false;
+              break;
+            }
+            const uint32_t sbase = smem_base + stage * STAGE_BYTES;
+            const uint32_t fb = tc::mapa_shared(full_bar(stage), 0);
+            if (leader) tc::mbar_arrive_expect_tx(full_bar(stage), 2 * STAGE_BYTES);
+            tc::tma_load_2d_pair(sbase, &tm_q, fb, kc * 64, qg * 256 + static_cast<int>(rank) * PM);
+            tc::tma_load_2d_pair(sbase + A_TILE, &tm_x, fb, kc * 64, t * 256 + static_cast<int>(rank) * PH);
+            issued[stage] = true;
+            issued_phase[stage] = phase;
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
+      }
+      // Both CTAs' loads complete on the even CTA's barriers: it waits for
+      // every phase it armed before shared memory goes away; the odd CTA
+      // leaves only after the closing cluster barrier.
+      if (leader) {
+#pragma unroll
+        for (int s = 0; s < STAGES; ++s)
+          if (issued[s]) mbar_wait_quiet(full_bar(s), issued_phase[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_bf16(2 * PM, 2 * PH);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int item = cluster; ok && item < p.n_items; item += nclusters) {
+        const int split = item / p.T;
+        const int t0 = split * p.tiles_per_split;
+        const int t1 = min(p.nb, t0 + p.tiles_per_split);
+        for (int t = t0; ok && t < t1; ++t) {
+          if (!tc::mbar_wait(tempty_bar(acc), acc_phase ^ 1, s_abort)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * 2 * PH);
+          for (int kc = 0; kc < KC; ++kc) {
+            if (!tc::mbar_wait(full_bar(stage), phase, s_abort)) {
+              ok = false;
+              break;
+            }
+            tc::tc_fence_after();
+            const uint32_t sbase = smem_base + stage * STAGE_BYTES;
+            const uint64_t a_desc = tc::sw128_kmajor_desc(sbase);
+            const uint64_t b_desc = tc::sw128_kmajor_desc(sbase + A_TILE);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t off = static_cast<uint64_t>(kk * 32) >> 4;
+              tc::mma_bf16_pair(d_tmem, a_desc + off, b_desc + off, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+            }
+            tc::mma_commit_pair(tc::mapa_shared(empty_bar(stage), 0));
+            tc::mma_commit_pair(tc::mapa_shared(empty_bar(stage), 1));
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+          if (!ok) break;
+          tc::mma_commit_pair(tc::mapa_shared(tfull_bar(acc), 0));
+          tc::mma_commit_pair(tc::mapa_shared(tfull_bar(acc), 1));
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1;
+          }
+        }
+      }
+      // Every issued MMA completes before either CTA releases TMEM or
+      // shared memory.
+      tc::mma_commit_pair(tc::mapa_shared(done_bar, 0));
+      tc::mma_commit_pair(tc::mapa_shared(done_bar, 1));
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int half = (warp - 2) >> 2;  // which 128 columns of each tile
+    const int quarter = warp & 3;      // TMEM lanes this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+    float slot[32];  // local memory, touched only on the rare insertion path
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int item = cluster; ok && item < p.n_items; item += nclusters) {
+      const int qg = item % p.T;
+      const int split = item / p.T;
+      const int t0 = split * p.tiles_per_split;
+      const int t1 = min(p.nb, t0 + p.tiles_per_split);
+      uint64_t L[CAP];
+#pragma unroll
+      for (int j = 0; j < CAP; ++j) L[j] = PX_EMPTY;
+      uint64_t thr = PX_EMPTY;
+      float thr_key = __int_as_float(0x7f800000);  // +inf: accept everything at first
+      int maxpos = 0;
+      for (int t = t0; t < t1; ++t) {
+        const bool got = __all_sync(0xffffffffu, tc::mbar_wait(tfull_bar(acc), acc_phase, s_abort, 256));
+        if (!got) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const int64_t row0 = static_cast<int64_t>(t) * (2 * PH) + half * PH;
+        const int64_t rem = p.n - row0;
+        const int valid_cols = rem < PH ? (rem < 0 ? 0 : static_cast<int>(rem)) : PH;
+        const uint32_t col0 = static_cast<uint32_t>(acc * 2 * PH + half * PH);
+        drain_columns<CAP, L2, PH>(L, thr, thr_key, maxpos, lane_addr + col0, row0, valid_cols, p, slot);
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive_cluster(tc::mapa_shared(tempty_bar(acc), 0));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      list_sort<CAP>(L);
+      const int64_t qidx = static_cast<int64_t>(qg) * (2 * PM) + static_cast<int64_t>(rank) * PM + row_in_tile;
+      if (qidx < p.nq) {
+        uint64_t* out = p.partial + ((qidx * p.S + split) * 2 + half) * CAP;
+#pragma unroll
+        for (int j = 0; j < CAP; ++j) out[j] = L[j];
+      }
+    }
+  }
+
+  if (warp == 1 && lane == 0) mbar_wait_quiet(done_bar, 0);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::cluster_sync();  // neither CTA leaves while the pair's MMAs or loads may touch it
+  tc::tc_fence_after();
+  if (warp == 1) tc::tmem_dealloc_pair(tmem_base, kTmemCols);
+  if (threadIdx.x == 0 && *s_abort) atomicOr(p.err, 1);
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -431,6 +701,17 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
   }
   return fn;
+}
+
+template <bool L2>
+cudaError_t launch_pair(const GemmTopkArgs& a, const CUtensorMap* maps, int grid, cudaStream_t stream) {
+  auto kern = gemm_topk_pair_kernel<L2, kPairCap>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(pairk::SMEM));
+  if (e != cudaSuccess) return e;
+  if (grid < 2 || grid % 2 != 0) return cudaErrorInvalidValue;
+  kern<<<grid, pairk::THREADS, pairk::SMEM, stream>>>(maps[0], maps[1], a);
+  return cudaGetLastError();
 }
 
 template <int CAP, bool L2, int QT, int KIND>
@@ -482,6 +763,30 @@ cudaError_t encode_bf16_map(CUtensorMap* map, const void* plane, int64_t rows, i
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+int gemm_pair_cap() { return kPairCap; }
+
+int gemm_pair_clusters(int device) {
+  static int cached[64] = {};
+  if (device < 0 || device >= 64) return 1;
+  if (cached[device] > 0) return cached[device];
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  int clusters = 0;
+  auto kern = gemm_topk_pair_kernel<false, kPairCap>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pairk::SMEM)) ==
+      cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(sms / 2 * 2), 1, 1);
+    cfg.blockDim = dim3(pairk::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = pairk::SMEM;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) clusters = 0;
+  }
+  cudaGetLastError();
+  if (clusters <= 0) clusters = sms / 2;
+  cached[device] = clusters;
+  return clusters;
+}
+
 int gemm_cap_for(int k) {
   if (k <= 16) return 32;
   if (k <= 224) return 64;
@@ -510,9 +815,12 @@ cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const void* q_plane, int64_t
   CUtensorMap maps[2];
   cudaError_t e;
   if (kind == kPassBf16) {
-    if (cap != 32) return cudaErrorInvalidValue;
-    e = encode_bf16_map(&maps[0], q_plane, q_rows, a.ldb, BM);
-    if (e == cudaSuccess) e = encode_bf16_map(&maps[1], x_plane, a.n, a.ldb, 256 / qt);
+    // CTA pairs: each CTA stages 128 query rows and 128 base rows per slice.
+    if (cap != 32) return cudaErrorInvalidValue;  // k <= 16
+    e = encode_bf16_map(&maps[0], q_plane, q_rows, a.ldb, pairk::PM);
+    if (e == cudaSuccess) e = encode_bf16_map(&maps[1], x_plane, a.n, a.ldb, pairk::PH);
+    if (e != cudaSuccess) return e;
+    return a.l2 ? launch_pair<true>(a, maps, grid, stream) : launch_pair<false>(a, maps, grid, stream);
   } else {
     const bool il = kind == kPass3xTf32;
     e = encode_split_map(&maps[0], static_cast<const float*>(q_plane), q_rows, a.ld, BM, il);
@@ -527,9 +835,6 @@ cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const void* q_plane, int64_t
       case kPassTf32:
         return a.l2 ? launch_typed<32, true, 2, kPassTf32>(a, maps, grid, stream)
                     : launch_typed<32, false, 2, kPassTf32>(a, maps, grid, stream);
-      case kPassBf16:
-        return a.l2 ? launch_typed<32, true, 2, kPassBf16>(a, maps, grid, stream)
-                    : launch_typed<32, false, 2, kPassBf16>(a, maps, grid, stream);
     }
   }
   if (cap == 64) {

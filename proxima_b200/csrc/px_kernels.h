@@ -135,9 +135,16 @@ int gemm_cap_for(int k);    // candidates kept per (query, split) in registers (
 int gemm_cands_for(int k);  // candidates per query after the split merge (<= 256)
 int gemm_qt_for(int k);   // query tiles of 128 per CTA (2 for k <= 16, else 1)
 int gemm_bn_for(int k);   // base rows per tile (256 / qt)
+// CTA pairs of the bf16 pass's kernel that fit on `device` at once (each
+// pair takes 256 queries x 256 base rows per tile, two lists per split).
+int gemm_pair_clusters(int device);
+int gemm_pair_cap();  // candidates per list of the pair kernel (the bf16 pass)
 // q_plane / x_plane: the interleaved split planes (stride 2*ld) for the tf32
 // passes, the bf16 planes (stride ldb) for kPassBf16, which serves
-// gemm_cap_for(k) == 32 only. kPassTf32 reads only the hi halves.
+// gemm_cap_for(k) == 32 only and runs on CTA pairs: grid is then an even
+// number of CTAs, T counts groups of 256 queries, nb tiles of 256 rows, and
+// partial holds two lists per split ([nq][S][2][cap]). kPassTf32 reads only
+// the hi halves.
 cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const void* q_plane, int64_t q_rows,
                              const void* x_plane, PassKind kind, int grid, cudaStream_t stream);
 

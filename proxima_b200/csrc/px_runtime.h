@@ -152,6 +152,7 @@ struct SearchPlan {
   int64_t rows_per_cta = 0;
   // tensor-core path
   int cap = 0, cands = 0, T = 0, S = 0, nb = 0, tiles_per_split = 0, n_items = 0, grid = 0;
+  int lists = 0;  // candidate lists per query: S, or 2 * S on CTA pairs
   int64_t q_rows = 0;
   size_t ws_bytes = 0;
   uint64_t* partial = nullptr;

@@ -39,30 +39,34 @@ int64_t gcd64(int64_t a, int64_t b) {
 
 }  // namespace
 
-// Work split of one tensor-core candidate pass over nq queries.
-static void plan_gemm(const FlatShard& sh, int64_t nq, int k, SearchPlan& plan) {
+// Work split of one tensor-core candidate pass over nq queries. Workers are
+// the persistent CTAs (one per SM), or CTA pairs for the bf16 pass.
+static void plan_gemm(const FlatShard& sh, int64_t nq, int k, PassKind kind, SearchPlan& plan) {
   plan.path = FlatPath::Gemm;
-  plan.cap = gemm_cap_for(k);
+  const bool pair = kind == kPassBf16;
+  plan.cap = pair ? gemm_pair_cap() : gemm_cap_for(k);
   plan.cands = gemm_cands_for(k);
-  // Work items: (group of QT query tiles, run of base tiles of BN rows).
-  const int qt = gemm_qt_for(k);
-  const int bn = gemm_bn_for(k);
-  const int64_t T = ((nq + 127) / 128 + qt - 1) / qt;
+  // Work items: (group of query tiles, run of base tiles).
+  const int64_t group_rows = pair ? 256 : static_cast<int64_t>(gemm_qt_for(k)) * 128;
+  const int64_t bn = pair ? 256 : gemm_bn_for(k);
+  const int64_t workers = pair ? gemm_pair_clusters(sh.device) : sh.sms;
+  const int64_t T = (nq + group_rows - 1) / group_rows;
   const int64_t nb = std::max<int64_t>(1, (sh.n + bn - 1) / bn);
-  // Splits so that T * S is a whole number of waves of one CTA per SM.
-  int64_t S = sh.sms / gcd64(T, sh.sms);
-  while (S * 2 <= 1024 && S * T < 2 * sh.sms && S * 2 <= nb) S *= 2;
+  // Splits so that T * S is a whole number of waves of the workers.
+  int64_t S = workers / gcd64(T, workers);
+  while (S * 2 <= 1024 && S * T < 2 * workers && S * 2 <= nb) S *= 2;
   S = std::min<int64_t>(S, nb);
   S = std::max<int64_t>(S, 1);
   const int64_t tps = (nb + S - 1) / S;
   S = (nb + tps - 1) / tps;
   plan.T = static_cast<int>(T);
   plan.S = static_cast<int>(S);
+  plan.lists = static_cast<int>(pair ? 2 * S : S);
   plan.nb = static_cast<int>(nb);
   plan.tiles_per_split = static_cast<int>(tps);
   plan.n_items = static_cast<int>(T * S);
-  plan.grid = static_cast<int>(std::min<int64_t>(sh.sms, T * S));
-  plan.q_rows = T * qt * 128;
+  plan.grid = static_cast<int>(pair ? 2 * std::min<int64_t>(workers, T * S) : std::min<int64_t>(workers, T * S));
+  plan.q_rows = T * group_rows;
 }
 
 namespace {
@@ -91,7 +95,7 @@ void carve_tensor_ws(Carver& c, const SearchPlan& plan, int64_t nq, int ld, int 
     w.qb = c.take(2 * static_cast<size_t>(plan.q_rows) * ldb);
   else
     w.q_hl = static_cast<float*>(c.take(sizeof(float) * static_cast<size_t>(plan.q_rows) * 2 * ld));
-  w.partial = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.S * plan.cap));
+  w.partial = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.lists * plan.cap));
   w.merged = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.cands));
   w.final_cands = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * k));
   w.status = static_cast<int*>(c.take(sizeof(int) * static_cast<size_t>(nq)));
@@ -123,7 +127,7 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
   if (nq > (int64_t(1) << 30)) return set_error(PX_EUNSUPPORTED, "too many queries in one call");
   Carver c;
   if (gemm) {
-    plan_gemm(sh, nq, k, plan);
+    plan_gemm(sh, nq, k, first_pass_for(k), plan);
     TensorWs w;
     carve_tensor_ws(c, plan, nq, h->ld, h->ldb, k, first_pass_for(k), w);
     if (masked) c.take(sizeof(uint32_t) * mask_words(sh.n));
@@ -251,7 +255,7 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
     e = launch_gemm_topk(g, w.q_hl, plan.q_rows, sh.hl, kind, plan.grid, stream);
   if (profile_main) cudaEventRecord(sh.ev_stop, stream);
   if (e != cudaSuccess) return cuda_status(e, "tensor-core kernel launch");
-  e = launch_merge_lists(w.partial, nq, plan.S, plan.cap, plan.cands, w.merged, stream);
+  e = launch_merge_lists(w.partial, nq, plan.lists, plan.cap, plan.cands, w.merged, stream);
   if (e != cudaSuccess) return cuda_status(e, "split merge launch");
   RescoreArgs r;
   r.merged = w.merged;
@@ -259,7 +263,7 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
   r.cap = plan.cands;
   r.k = k;
   r.lists = w.partial;
-  r.nlists = plan.S;
+  r.nlists = plan.lists;
   r.list_cap = plan.cap;
   r.queries = d_q;
   r.base = sh.x;
@@ -335,7 +339,7 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   if (n_fail > 0) {
     if (inexact && refine_pays(n_fail, k)) {
       SearchPlan p2;
-      plan_gemm(sh, n_fail, k, p2);
+      plan_gemm(sh, n_fail, k, kPass3xTf32, p2);
       Carver c2;
       c2.take(sizeof(float) * static_cast<size_t>(n_fail) * h->dim);
       TensorWs w2;
