@@ -442,8 +442,8 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 // outputs, against 384 rows for 256 x 128 outputs in the single-CTA kernel:
 // 1.5x less operand traffic from L2 per output.
 //
-// Barriers (no multicast anywhere; the even CTA commits to each CTA's
-// barrier separately):
+// Barriers (no TMA load uses multicast; the even CTA's tcgen05.commit signals
+// the barrier at the same offset in both CTAs):
 //   full[s]   even CTA; armed by its producer for both CTAs' bytes, and both
 //             CTAs' TMA loads complete on it
 //   empty[s]  each CTA; stage s consumed by the MMAs
@@ -608,16 +608,14 @@ gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
               const uint64_t off = static_cast<uint64_t>(kk * 32) >> 4;
               tc::mma_bf16_pair(d_tmem, a_desc + off, b_desc + off, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
             }
-            tc::mma_commit_pair(tc::mapa_shared(empty_bar(stage), 0));
-            tc::mma_commit_pair(tc::mapa_shared(empty_bar(stage), 1));
+            tc::mma_commit_pair_both(empty_bar(stage));
             if (++stage == STAGES) {
               stage = 0;
               phase ^= 1;
             }
           }
           if (!ok) break;
-          tc::mma_commit_pair(tc::mapa_shared(tfull_bar(acc), 0));
-          tc::mma_commit_pair(tc::mapa_shared(tfull_bar(acc), 1));
+          tc::mma_commit_pair_both(tfull_bar(acc));
           if (++acc == 2) {
             acc = 0;
             acc_phase ^= 1;
@@ -626,8 +624,7 @@ gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       }
       // Every issued MMA completes before either CTA releases TMEM or
       // shared memory.
-      tc::mma_commit_pair(tc::mapa_shared(done_bar, 0));
-      tc::mma_commit_pair(tc::mapa_shared(done_bar, 1));
+      tc::mma_commit_pair_both(done_bar);
     }
   } else {
     // ------------------------------------------------------------ epilogue

@@ -282,11 +282,14 @@ __device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, 
       : "memory");
 }
 
-// Arrives on the mbarrier at `cluster_bar` (either CTA of the pair) once the
-// pair MMAs issued so far by this thread are done.
-__device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
-               : "memory");
+// Arrives on the mbarrier at shared address `bar` in both CTAs of the pair
+// once the pair MMAs issued so far by this thread are done (one commit
+// signalling both CTAs; this is a completion signal, not a load).
+__device__ __forceinline__ void mma_commit_pair_both(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(static_cast<unsigned short>(3))
+      : "memory");
 }
 
 // Instruction descriptor: D f32, A/B bf16 (kind::f16), both K-major, M x N.
