@@ -467,12 +467,9 @@ constexpr int THREADS = 64 + 256;
 constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + NBARS * 8 + 16;
 }  // namespace pairk
 
-// Candidates kept per (query, split, column half) by the pair kernel. A list
-// over ~10^5 rows refills ~CAP * ln(rows / CAP) times at a cost linear in CAP,
-// while the merge needs only the best 64 per query across all lists (spread
-// ~1 per list): 16 keeps every k <= 16 certifiable even when one list holds
-// all the neighbours, at a quarter of the insertion work of 32.
-constexpr int kPairCap = 16;
+// Largest k the bf16 pass serves (its candidates then number 256, the most
+// the rescoring takes; beyond, the bf16 bound is too wide to certify).
+constexpr int kPairMaxK = 100;
 
 template <bool L2, int CAP>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairk::THREADS, 1)
@@ -700,9 +697,9 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-template <bool L2>
+template <bool L2, int CAP>
 cudaError_t launch_pair(const GemmTopkArgs& a, const CUtensorMap* maps, int grid, cudaStream_t stream) {
-  auto kern = gemm_topk_pair_kernel<L2, kPairCap>;
+  auto kern = gemm_topk_pair_kernel<L2, CAP>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(pairk::SMEM));
   if (e != cudaSuccess) return e;
@@ -760,7 +757,26 @@ cudaError_t encode_bf16_map(CUtensorMap* map, const void* plane, int64_t rows, i
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-int gemm_pair_cap() { return kPairCap; }
+// Candidates kept per (query, split, column half) by the pair kernel. A list
+// over ~10^5 rows refills ~CAP * ln(rows / CAP) times at a cost linear in CAP,
+// while the merge needs only the best few per query from each of ~74 lists:
+// 16 keeps every k <= 16 certifiable even when one list holds all the
+// neighbours, at a quarter of the insertion work of 32; larger k keep 32.
+int gemm_pair_cap(int k) { return k <= 16 ? 16 : 32; }
+
+// Candidates rescored per query after a bf16 pass. The certificate compares
+// the k-th exact key with the largest approximate key among them, so more
+// candidates widen the margin it can prove. On config 4's distribution
+// (20,000 simulated queries each): k = 10 leaves 0.07% uncertified with 32
+// and none with 64; k = 32 leaves 4.8% with 64 and none with 128; k = 50
+// none with 128; k = 100 61% with 160 and none with 256.
+int gemm_pair_cands(int k) {
+  if (k > kPairMaxK) return 0;
+  if (k <= 16) return 64;
+  if (k <= 50) return 128;
+  return 256;
+}
+
 
 int gemm_pair_clusters(int device) {
   static int cached[64] = {};
@@ -769,7 +785,7 @@ int gemm_pair_clusters(int device) {
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   int clusters = 0;
-  auto kern = gemm_topk_pair_kernel<false, kPairCap>;
+  auto kern = gemm_topk_pair_kernel<false, 16>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pairk::SMEM)) ==
       cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
@@ -790,10 +806,7 @@ int gemm_cap_for(int k) {
   return 0;
 }
 
-// Candidates rescored per query. The certificate compares the k-th exact key
-// with the largest approximate key among them, so more candidates widen the
-// margin it can prove: with bf16 candidates for config 4's distribution,
-// 32 leave ~0.07% of queries uncertified and 64 none in 20,000 trials.
+// Candidates rescored per query after a tf32 pass (see gemm_pair_cands).
 int gemm_cands_for(int k) {
   if (k <= 40) return 64;
   if (k <= 224) return (k + 32 + 31) / 32 * 32;
@@ -813,11 +826,13 @@ cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const void* q_plane, int64_t
   cudaError_t e;
   if (kind == kPassBf16) {
     // CTA pairs: each CTA stages 128 query rows and 128 base rows per slice.
-    if (cap != 32) return cudaErrorInvalidValue;  // k <= 16
+    if (a.k > kPairMaxK) return cudaErrorInvalidValue;
     e = encode_bf16_map(&maps[0], q_plane, q_rows, a.ldb, pairk::PM);
     if (e == cudaSuccess) e = encode_bf16_map(&maps[1], x_plane, a.n, a.ldb, pairk::PH);
     if (e != cudaSuccess) return e;
-    return a.l2 ? launch_pair<true>(a, maps, grid, stream) : launch_pair<false>(a, maps, grid, stream);
+    if (gemm_pair_cap(a.k) == 16)
+      return a.l2 ? launch_pair<true, 16>(a, maps, grid, stream) : launch_pair<false, 16>(a, maps, grid, stream);
+    return a.l2 ? launch_pair<true, 32>(a, maps, grid, stream) : launch_pair<false, 32>(a, maps, grid, stream);
   } else {
     const bool il = kind == kPass3xTf32;
     e = encode_split_map(&maps[0], static_cast<const float*>(q_plane), q_rows, a.ld, BM, il);

@@ -138,10 +138,11 @@ int gemm_bn_for(int k);   // base rows per tile (256 / qt)
 // CTA pairs of the bf16 pass's kernel that fit on `device` at once (each
 // pair takes 256 queries x 256 base rows per tile, two lists per split).
 int gemm_pair_clusters(int device);
-int gemm_pair_cap();  // candidates per list of the pair kernel (the bf16 pass)
+int gemm_pair_cap(int k);    // candidates per list of the pair kernel (the bf16 pass)
+int gemm_pair_cands(int k);  // candidates per query after a bf16 pass (0: k too large for it)
 // q_plane / x_plane: the interleaved split planes (stride 2*ld) for the tf32
 // passes, the bf16 planes (stride ldb) for kPassBf16, which serves
-// gemm_cap_for(k) == 32 only and runs on CTA pairs: grid is then an even
+// gemm_pair_cands(k) > 0 only and runs on CTA pairs: grid is then an even
 // number of CTAs, T counts groups of 256 queries, nb tiles of 256 rows, and
 // partial holds two lists per split ([nq][S][2][cap]). kPassTf32 reads only
 // the hi halves.

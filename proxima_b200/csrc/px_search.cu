@@ -44,8 +44,8 @@ int64_t gcd64(int64_t a, int64_t b) {
 static void plan_gemm(const FlatShard& sh, int64_t nq, int k, PassKind kind, SearchPlan& plan) {
   plan.path = FlatPath::Gemm;
   const bool pair = kind == kPassBf16;
-  plan.cap = pair ? gemm_pair_cap() : gemm_cap_for(k);
-  plan.cands = gemm_cands_for(k);
+  plan.cap = pair ? gemm_pair_cap(k) : gemm_cap_for(k);
+  plan.cands = pair ? gemm_pair_cands(k) : gemm_cands_for(k);
   // Work items: (group of query tiles, run of base tiles).
   const int64_t group_rows = pair ? 256 : static_cast<int64_t>(gemm_qt_for(k)) * 128;
   const int64_t bn = pair ? 256 : gemm_bn_for(k);
@@ -84,10 +84,10 @@ struct TensorWs {
                                     // [3] some query value inexact in bf16
 };
 
-// The first candidate pass: bf16 where the candidate lists are short enough
-// for its wider bound to certify typical data (k <= 16), tf32 hi values
+// The first candidate pass: bf16 where enough candidates can be rescored for
+// its wider bound to certify typical data (k <= 100), tf32 hi values
 // otherwise.
-PassKind first_pass_for(int k) { return gemm_cap_for(k) == 32 ? kPassBf16 : kPassTf32; }
+PassKind first_pass_for(int k) { return gemm_pair_cands(k) > 0 ? kPassBf16 : kPassTf32; }
 
 void carve_tensor_ws(Carver& c, const SearchPlan& plan, int64_t nq, int ld, int ldb, int k, PassKind kind,
                      TensorWs& w) {
