@@ -473,10 +473,11 @@ def run_ours(args, cfg, rank, world, local_rank):
             roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                         "frac": achieved / peak, "traffic": traffic,
                         "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
-                                        "(profiles/gemm_topk_kernel.md)" if traffic else None,
-                        "kernel": "gemm_topk_kernel (tcgen05 " + ("kind::f16, bf16 operands"
-                                                                  if first == "bf16" else
-                                                                  "kind::tf32, hi values") + ")",
+                                        "(profiles/gemm_topk_c4k10_launches.md); the bf16 base is "
+                                        f"{2 * n_local * dim / 1e9:.2f} GB" if traffic else None,
+                        "kernel": ("gemm_topk_pair_kernel (tcgen05 cta_group::2 kind::f16, bf16 operands)"
+                                   if first == "bf16" else
+                                   "gemm_topk_kernel (tcgen05 kind::tf32, hi values)"),
                         "kernel_ms": statistics.mean(kernel_ms),
                         "peak_basis": (f"bf16 rate = bf16_tflops_sustained {pk['bf16_tflops_sustained']}, "
                                        if first == "bf16" else
