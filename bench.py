@@ -372,6 +372,7 @@ def run_ours(args, cfg, rank, world, local_rank):
     index = ShardedFlatIndex(dim, m, device=local_rank)
     begin, end = shard_range(n, world, rank)
     index.set_offset(begin)
+    index.local.set_search_path(args.path)
     index.reserve_local(end - begin)
     t0 = time.time()
     gen_rows(kind, begin, end, dim, args.seed, device, index.add_local_device)
@@ -467,23 +468,30 @@ def run_ours(args, cfg, rank, world, local_rank):
             flops = 2.0 * nq * n_local * dim
             achieved = flops / avg_s / 1e12
             first = index.local.last_search_profile()["first_pass"]
-            # bf16 MMAs issue at the measured bf16 rate, tf32 at half of it.
-            peak = pk["bf16_tflops_sustained"] / (1.0 if first == "bf16" else 2.0)
+            # bf16 MMAs issue at the measured bf16 rate, tf32 at half of it,
+            # and the 3xTF32 sum takes three tf32 MMAs per product.
+            peak = pk["bf16_tflops_sustained"] / {"bf16": 1.0, "tf32": 2.0, "3xtf32": 6.0}[first]
+            fp32_peak = pk["bf16_tflops_sustained"] / 6.0
             traffic = ncu_traffic(args.config, "gemm_topk_kernel") if world == 1 else None
             roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                         "frac": achieved / peak, "traffic": traffic,
                         "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
                                         "(profiles/gemm_topk_c4k10_launches.md); the bf16 base is "
                                         f"{2 * n_local * dim / 1e9:.2f} GB" if traffic else None,
-                        "kernel": ("gemm_topk_pair_kernel (tcgen05 cta_group::2 kind::f16, bf16 operands)"
-                                   if first == "bf16" else
-                                   "gemm_topk_kernel (tcgen05 kind::tf32, hi values)"),
+                        "kernel": {"bf16": "gemm_topk_pair_kernel (tcgen05 cta_group::2 kind::f16, bf16 operands)",
+                                   "tf32": "gemm_topk_kernel (tcgen05 kind::tf32, hi values)",
+                                   "3xtf32": "gemm_topk_kernel (tcgen05 kind::tf32, 3xTF32 sum)"}[first],
                         "kernel_ms": statistics.mean(kernel_ms),
-                        "peak_basis": (f"bf16 rate = bf16_tflops_sustained {pk['bf16_tflops_sustained']}, "
-                                       if first == "bf16" else
-                                       f"TF32 rate = bf16_tflops_sustained {pk['bf16_tflops_sustained']} "
-                                       f"/ 2 (tf32 MMA rate), ") + pk["source"],
+                        "peak_basis": {"bf16": "bf16 rate = bf16_tflops_sustained",
+                                       "tf32": "TF32 rate = bf16_tflops_sustained / 2",
+                                       "3xtf32": "3xTF32 rate = bf16_tflops_sustained / 2 / 3"}[first]
+                                      + f" ({pk['bf16_tflops_sustained']}), " + pk["source"],
                         "frac_of_bf16_peak": achieved / pk["bf16_tflops_sustained"],
+                        # Exact kNN throughput against the fp32-accurate (3xTF32)
+                        # tensor roofline: the results are exact on every path.
+                        "vs_fp32_accurate_roofline": {"achieved_tflops": achieved, "peak_tflops": fp32_peak,
+                                                      "frac": achieved / fp32_peak,
+                                                      "basis": "3xTF32 rate = bf16_tflops_sustained / 2 / 3"},
                         "algorithmic_flops_per_launch": flops}
         else:
             byts = 4.0 * n_local * dim
@@ -546,6 +554,8 @@ def main(argv=None):
     ap.add_argument("--cpu-sample", type=int, default=32, help="queries timed on the CPU baseline")
     ap.add_argument("--ref-sample", type=int, default=16, help="queries per step of --impl reference")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--path", choices=["auto", "exact", "tensor", "tensor_3xtf32"], default="auto",
+                    help="flat-search kernel path (auto is the library default)")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "ours":
         print("note: --warmup raised to 3 (timing rule)", file=sys.stderr)

@@ -109,8 +109,10 @@ PX_API px_status px_flat_read_rows(const px_flat* h, int64_t start, int64_t coun
 /* Kernel path for flat searches: AUTO picks the exact streaming scan for
  * small batches and the tensor-core path otherwise; EXACT and
  * TENSOR force one (TENSOR fails with PX_EUNSUPPORTED where it cannot serve
- * the request, e.g. k > 224). Masks work on both paths. Results are identical on every path. */
-enum { PX_PATH_AUTO = 0, PX_PATH_EXACT = 1, PX_PATH_TENSOR = 2 };
+ * the request, e.g. k > 224). TENSOR_3XTF32 is TENSOR with the first
+ * candidate pass in 3xTF32 (~fp32-accurate candidates) instead of bf16/tf32.
+ * Masks work on every path. Results are identical on every path. */
+enum { PX_PATH_AUTO = 0, PX_PATH_EXACT = 1, PX_PATH_TENSOR = 2, PX_PATH_TENSOR_3XTF32 = 3 };
 PX_API px_status px_flat_set_path(px_flat* h, int32_t mode);
 
 /* Per-search instrumentation (off by default). With profiling on, the

@@ -223,12 +223,14 @@ class FlatIndex:
         """The px_flat* handle (for callers that drive the C ABI directly)."""
         return self._h
 
-    _PATHS = {"auto": 0, "exact": 1, "tensor": 2}
+    _PATHS = {"auto": 0, "exact": 1, "tensor": 2, "tensor_3xtf32": 3}
 
     def set_search_path(self, path: str) -> None:
         """Kernel path for searches: "auto" (default), "exact" (streaming
-        scan) or "tensor" (tcgen05 3xTF32 + exact rescoring). Results are
-        identical on every path; this only changes speed."""
+        scan), "tensor" (tcgen05 candidates -- bf16 for k <= 100, tf32 above --
+        then exact rescoring) or "tensor_3xtf32" (the same with ~fp32-accurate
+        3xTF32 candidates). Results are identical on every path; this only
+        changes speed."""
         _lib.check(self._lib.px_flat_set_path(self._h, self._PATHS[path]))
 
     def last_search_profile(self) -> dict:

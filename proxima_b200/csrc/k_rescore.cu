@@ -52,16 +52,37 @@ rescore_kernel(const RescoreArgs a) {
   for (int off = 16; off > 0; off >>= 1) qsq += __shfl_xor_sync(0xffffffffu, qsq, off);
   __syncwarp();
 
+  // Exact keys, four candidates at a time: thread l of a group of eight runs
+  // the reference's lane-l accumulator (acc_l += term(x[8c + l], q[8c + l]),
+  // c = 0, 1, ...) on its own, so each accumulator is the same sequential
+  // chain as the reference's, and the group reads 32 contiguous bytes of the
+  // row per step. The lanes are then summed left to right and the remainder
+  // added, as distance.rs does.
   const uint64_t* mq = a.merged + q * a.cap;
-  for (int j = lane; j < a.cap; j += 32) {
-    const uint64_t c = mq[j];
-    uint64_t e = PX_EMPTY;
-    if (c != PX_EMPTY) {
-      const uint32_t row = cand_row(c);
-      const float key = exact_key<L2>(s_q, a.base + static_cast<int64_t>(row) * a.ld, a.d);
-      e = pack_cand(key, row);
+  const int grp = lane >> 3, l = lane & 7, g0 = lane & ~7;
+  const int chunks = a.d >> 3;
+  for (int j0 = 0; j0 < a.cap; j0 += 4) {
+    const int j = j0 + grp;
+    const uint64_t c = j < a.cap ? mq[j] : PX_EMPTY;
+    const bool valid = c != PX_EMPTY;
+    const uint32_t row = valid ? cand_row(c) : 0u;
+    const float* x = a.base + static_cast<int64_t>(row) * a.ld;
+    float acc = 0.f;
+    if (valid) {
+#pragma unroll 4
+      for (int cc = 0; cc < chunks; ++cc) acc = __fadd_rn(acc, lane_term<L2>(s_q[cc * 8 + l], x[cc * 8 + l]));
     }
-    s_c[j] = e;
+    float sum = __shfl_sync(0xffffffffu, acc, g0);
+#pragma unroll
+    for (int m = 1; m < 8; ++m) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, acc, g0 + m));
+    if (l == 0 && j < a.cap) {
+      uint64_t e = PX_EMPTY;
+      if (valid) {
+        for (int i = chunks * 8; i < a.d; ++i) sum = __fadd_rn(sum, lane_term<L2>(s_q[i], x[i]));
+        e = pack_cand(L2 ? sum : -sum, row);
+      }
+      s_c[j] = e;
+    }
   }
   __syncwarp();
   // Rank sort (values are distinct except PX_EMPTY; equal ones rank by index).

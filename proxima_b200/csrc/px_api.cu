@@ -373,8 +373,9 @@ PX_API int32_t px_flat_metric(const px_flat* h) { return h ? h->metric : -1; }
 PX_API px_status px_flat_set_path(px_flat* h, int32_t mode) {
   px_status s = flat_check(h);
   if (s != PX_OK) return s;
-  if (mode != PX_PATH_AUTO && mode != PX_PATH_EXACT && mode != PX_PATH_TENSOR)
-    return set_error(PX_EINVAL, "path mode must be PX_PATH_AUTO, PX_PATH_EXACT or PX_PATH_TENSOR");
+  if (mode != PX_PATH_AUTO && mode != PX_PATH_EXACT && mode != PX_PATH_TENSOR && mode != PX_PATH_TENSOR_3XTF32)
+    return set_error(PX_EINVAL,
+                     "path mode must be PX_PATH_AUTO, PX_PATH_EXACT, PX_PATH_TENSOR or PX_PATH_TENSOR_3XTF32");
   h->path_mode = mode;
   return PX_OK;
 }

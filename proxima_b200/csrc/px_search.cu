@@ -87,7 +87,10 @@ struct TensorWs {
 // The first candidate pass: bf16 where enough candidates can be rescored for
 // its wider bound to certify typical data (k <= 100), tf32 hi values
 // otherwise.
-PassKind first_pass_for(int k) { return gemm_pair_cands(k) > 0 ? kPassBf16 : kPassTf32; }
+PassKind first_pass_for(const px_flat* h, int k) {
+  if (h->path_mode == PX_PATH_TENSOR_3XTF32) return kPass3xTf32;
+  return gemm_pair_cands(k) > 0 ? kPassBf16 : kPassTf32;
+}
 
 void carve_tensor_ws(Carver& c, const SearchPlan& plan, int64_t nq, int ld, int ldb, int k, PassKind kind,
                      TensorWs& w) {
@@ -122,14 +125,15 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
   bool gemm = cap > 0 && h->ld % 32 == 0 && sh.hl != nullptr;
   if (h->path_mode == PX_PATH_EXACT) gemm = false;
   if (h->path_mode == PX_PATH_AUTO) gemm = gemm && nq >= kGemmMinQueries && sh.n >= kGemmMinRows;
-  if (h->path_mode == PX_PATH_TENSOR && !gemm)
+  if ((h->path_mode == PX_PATH_TENSOR || h->path_mode == PX_PATH_TENSOR_3XTF32) && !gemm)
     return set_error(PX_EUNSUPPORTED, "the tensor-core path cannot serve this request (k, mask or layout)");
   if (nq > (int64_t(1) << 30)) return set_error(PX_EUNSUPPORTED, "too many queries in one call");
   Carver c;
   if (gemm) {
-    plan_gemm(sh, nq, k, first_pass_for(k), plan);
+    const PassKind first = first_pass_for(h, k);
+    plan_gemm(sh, nq, k, first, plan);
     TensorWs w;
-    carve_tensor_ws(c, plan, nq, h->ld, h->ldb, k, first_pass_for(k), w);
+    carve_tensor_ws(c, plan, nq, h->ld, h->ldb, k, first, w);
     if (masked) c.take(sizeof(uint32_t) * mask_words(sh.n));
   } else {
     plan.path = FlatPath::Exact;
@@ -322,7 +326,7 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   // 2. The uncertified queries, if that pass's operands were inexact and
   //    there are enough of them, get a three-pass (~fp32) candidate pass.
   // 3. Whatever is still uncertified goes through the exact scan.
-  const PassKind first = first_pass_for(k);
+  const PassKind first = first_pass_for(h, k);
   sh.last_pass = first;
   TensorWs w;
   carve_tensor_ws(c, plan, nq, h->ld, h->ldb, k, first, w);
@@ -337,7 +341,7 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   px_status s = tensor_pass(h, sh, plan, metric, d_q, nq, k, mask_bits, first, w, prof, stream, &n_fail, &inexact);
   if (s != PX_OK) return s;
   if (n_fail > 0) {
-    if (inexact && refine_pays(n_fail, k)) {
+    if (first != kPass3xTf32 && inexact && refine_pays(n_fail, k)) {
       SearchPlan p2;
       plan_gemm(sh, n_fail, k, kPass3xTf32, p2);
       Carver c2;

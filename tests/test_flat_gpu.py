@@ -270,19 +270,22 @@ def _run_path(pxm, data, metric, queries, k, path):
     return ids, d, idx.last_search_profile()
 
 
+@pytest.mark.parametrize("path", ["tensor", "tensor_3xtf32"])
 @pytest.mark.parametrize("metric", [O.L2, O.IP])
 @pytest.mark.parametrize("n,dim,nq,k", [
     (5000, 32, 16, 10), (20000, 64, 128, 10), (9000, 128, 300, 16), (12345, 24, 77, 1),
     (30000, 96, 200, 40), (8192, 768, 130, 10), (4096, 384, 129, 5),
     (20000, 64, 140, 100), (9000, 48, 33, 224), (12000, 128, 260, 41),
 ])
-def test_tensor_path_parity(pxm, metric, n, dim, nq, k):
+def test_tensor_path_parity(pxm, metric, n, dim, nq, k, path):
     data = _data.unit_gaussian(n, dim, n + dim) if metric == O.IP else \
         _data.gaussian_mixture(n, nq, d=dim, centres=50, seed=dim)[0]
     queries = _data.unit_gaussian(nq, dim, 7 * dim) if metric == O.IP else \
         _data.gaussian_mixture(10, nq, d=dim, centres=50, seed=dim)[1]
-    ids, d, prof = _run_path(pxm, data, metric, queries, k, "tensor")
+    ids, d, prof = _run_path(pxm, data, metric, queries, k, path)
     assert prof["path"] == "tensor"
+    expected = "3xtf32" if path == "tensor_3xtf32" else ("bf16" if k <= 100 else "tf32")
+    assert prof["first_pass"] == expected, prof
     _parity.check_flat(data, metric, queries, ids, d, k)
     # Exact-scan fallbacks are legal but must stay rare on generic data
     # (clustered L2 data leaves a few percent uncertified by the one-pass
