@@ -652,6 +652,13 @@ gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         }
         tc::tc_fence_after();
         const int64_t row0 = static_cast<int64_t>(t) * (2 * PH) + half * PH;
+        if (L2 && t + 1 < t1 && lane < PH / 32) {
+          // The next tile's 128 norms (four 128-byte lines, inside the
+          // norms' 256-row padding) into L1, so the key computation of the
+          // next tile does not wait on L2.
+          const float* nx = p.norms + row0 + 2 * PH + lane * 32;
+          asm volatile("prefetch.global.L1 [%0];" ::"l"(nx));
+        }
         const int64_t rem = p.n - row0;
         const int valid_cols = rem < PH ? (rem < 0 ? 0 : static_cast<int>(rem)) : PH;
         const uint32_t col0 = static_cast<uint32_t>(acc * 2 * PH + half * PH);
