@@ -63,7 +63,7 @@ template <int QT, int KIND> struct Tile {
   static constexpr int STAGE_BYTES = QT * A_TILE + B_TILE;
   static constexpr int NBARS = 2 * STAGES + 2 + 2 + 1;  // full, empty, tmem full, tmem empty, done
   static constexpr int THREADS = 64 + 128 * QT;  // TMA warp, MMA warp, QT epilogue warpgroups
-  static constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + NBARS * 8 + 16 + 128 * QT * 33 * 4;
+  static constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + NBARS * 8 + 16;
 };
 
 __device__ __forceinline__ bool mbar_wait_quiet(uint32_t bar, uint32_t parity) {
@@ -126,55 +126,92 @@ __device__ __forceinline__ void list_sort(uint64_t (&L)[CAP]) {
   }
 }
 
+// Approximate keys of 32 accumulator columns (base rows rbase ..): -q.x, or
+// ||x||^2 - 2 q.x with the row norms (padded to whole 256-row tiles, so every
+// chunk of a tile is in bounds).
+template <bool L2>
+__device__ __forceinline__ void chunk_keys(const uint32_t (&v)[32], const GemmTopkArgs& p, int64_t rbase,
+                                           float (&key)[32]) {
+  if (L2) {
+    const float4* nrm = reinterpret_cast<const float4*>(p.norms + rbase);
+#pragma unroll
+    for (int j4 = 0; j4 < 8; ++j4) {
+      const float4 nv = __ldg(nrm + j4);
+      key[4 * j4 + 0] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 0]), nv.x);
+      key[4 * j4 + 1] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 1]), nv.y);
+      key[4 * j4 + 2] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 2]), nv.z);
+      key[4 * j4 + 3] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 3]), nv.w);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) key[j] = -__uint_as_float(v[j]);
+  }
+}
+
+__device__ __forceinline__ uint32_t low_bits(int n) {
+  return n <= 0 ? 0u : (n >= 32 ? 0xffffffffu : (1u << n) - 1u);
+}
+
 // Drains NCOL accumulator columns (base rows row0 ..) of this thread's TMEM
-// lane into its top-CAP list: approximate keys, a three-input min tree that
-// rejects a 32-column chunk in the common case, and the exact per-column test
-// and insertion otherwise. taddr: the lane's TMEM address of column 0.
+// lane into its top-CAP list, 64 columns per step: two TMEM loads in flight
+// and one wait, approximate keys, two independent three-input min trees that
+// reject the 64 columns in the common case, and the exact per-column test and
+// insertion otherwise. taddr: the lane's TMEM address of column 0; slot: 64
+// floats of this thread (local memory), touched only on the rare path.
 template <int CAP, bool L2, int NCOL>
 __device__ __forceinline__ void drain_columns(uint64_t (&L)[CAP], uint64_t& thr, float& thr_key, int& maxpos,
                                               uint32_t taddr, int64_t row0, int valid_cols,
                                               const GemmTopkArgs& p, float* slot) {
+  static_assert(NCOL % 64 == 0, "columns are drained 64 at a time");
 #pragma unroll 1
-  for (int c = 0; c < NCOL / 32; ++c) {
-    __syncwarp();  // the tcgen05.ld below is .sync.aligned
-    uint32_t v[32];
-    tc::tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), v);
+  for (int c = 0; c < NCOL / 64; ++c) {
+    __syncwarp();  // tcgen05.ld is .sync.aligned
+    uint32_t v0[32], v1[32];
+    tc::tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 64), v0);
+    tc::tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 64 + 32), v1);
     tc::tmem_ld_wait();
-    const int64_t rbase = row0 + c * 32;
-    const int nvalid = valid_cols - c * 32;
+    const int64_t rbase = row0 + c * 64;
+    const int nvalid = valid_cols - c * 64;
     if (nvalid <= 0) continue;
-    // Hot path: the approximate keys of 32 columns.
-    float key[32];
-    if (L2) {
-      const float4* nrm = reinterpret_cast<const float4*>(p.norms + rbase);
+    float k0[32], k1[32];
+    chunk_keys<L2>(v0, p, rbase, k0);
+    chunk_keys<L2>(v1, p, rbase + 32, k1);
+    // Common case: nothing in the 64 columns beats the threshold. Partial or
+    // filtered steps take the exact per-column test; otherwise only a half
+    // whose minimum can pass does.
+    const float m0 = min32(k0), m1 = min32(k1);
+    const bool whole = nvalid >= 64 && p.mask_bits == nullptr;
+    if (whole && !(fminf(m0, m1) <= thr_key)) continue;
+    uint32_t pass0 = 0, pass1 = 0;
+    if (!whole || m0 <= thr_key) {
 #pragma unroll
-      for (int j4 = 0; j4 < 8; ++j4) {
-        const float4 nv = __ldg(nrm + j4);
-        key[4 * j4 + 0] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 0]), nv.x);
-        key[4 * j4 + 1] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 1]), nv.y);
-        key[4 * j4 + 2] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 2]), nv.z);
-        key[4 * j4 + 3] = fmaf(-2.0f, __uint_as_float(v[4 * j4 + 3]), nv.w);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) key[j] = -__uint_as_float(v[j]);
+      for (int j = 0; j < 32; ++j) pass0 |= (k0[j] <= thr_key ? 1u : 0u) << j;
     }
-    // Common case: nothing in the chunk beats the threshold, which one
-    // minimum over the 32 keys shows. Partial or filtered chunks take
-    // the exact per-column test.
-    if (nvalid == 32 && p.mask_bits == nullptr && !(min32(key) <= thr_key)) continue;
-    uint32_t pass = 0;
+    if (!whole || m1 <= thr_key) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) pass |= (key[j] <= thr_key ? 1u : 0u) << j;
-    if (nvalid < 32) pass &= (1u << nvalid) - 1u;
-    if (p.mask_bits) pass &= __ldg(p.mask_bits + (rbase >> 5));  // rbase is a multiple of 32
-    if (pass) {
-      // Rare path, one copy of the insertion code: keys go through
-      // this thread's slot (shared or local memory) so they can be indexed.
+      for (int j = 0; j < 32; ++j) pass1 |= (k1[j] <= thr_key ? 1u : 0u) << j;
+    }
+    pass0 &= low_bits(nvalid);
+    pass1 &= low_bits(nvalid - 32);
+    if (p.mask_bits) {  // rbase is a multiple of 64
+      pass0 &= __ldg(p.mask_bits + (rbase >> 5));
+      pass1 &= __ldg(p.mask_bits + (rbase >> 5) + 1);
+    }
+    if (pass0 | pass1) {
+      // Rare path, one copy of the insertion code: the keys of a half with
+      // a passing column go through this thread's slot so they can be
+      // indexed.
+      if (pass0) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) slot[j] = key[j];
+        for (int j = 0; j < 32; ++j) slot[j] = k0[j];
+      }
+      if (pass1) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) slot[32 + j] = k1[j];
+      }
+      uint64_t pass = static_cast<uint64_t>(pass0) | (static_cast<uint64_t>(pass1) << 32);
       while (pass) {
-        const int j = __ffs(pass) - 1;
+        const int j = __ffsll(static_cast<long long>(pass)) - 1;
         pass &= pass - 1;
         const float kj = slot[j];
         if (kj <= thr_key) {
@@ -206,7 +243,6 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + TL::NBARS);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
-  float* s_keys = reinterpret_cast<float*>(s_tmem + 4);  // (128 * QT) x 33 epilogue key slots
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -376,7 +412,7 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const int quarter = warp & 3;    // TMEM lanes this warp may access
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-    float* slot = s_keys + (wg * 128 + row_in_tile) * 33;
+    float slot[64];  // local memory, touched only on the rare insertion path
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
@@ -629,7 +665,7 @@ gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     const int quarter = warp & 3;      // TMEM lanes this warp may access
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-    float slot[32];  // local memory, touched only on the rare insertion path
+    float slot[64];  // local memory, touched only on the rare insertion path
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
