@@ -27,6 +27,15 @@ __device__ __forceinline__ float lds_f32(uint32_t addr) {
   return v;
 }
 
+// The same load, free for the compiler to schedule and to fold constant
+// offsets into. Only for addresses that depend on data loaded after the
+// table's __syncthreads (a code byte), so it cannot move above it.
+__device__ __forceinline__ float lds_f32_sched(uint32_t addr) {
+  float v;
+  asm("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+
 __global__ void pq_lut_kernel(const float* __restrict__ books, int m, int ksub, int dsub, bool l2,
                               const float* __restrict__ queries, float* __restrict__ lut) {
   const int q = blockIdx.x;
@@ -44,7 +53,9 @@ __global__ void pq_lut_kernel(const float* __restrict__ books, int m, int ksub, 
 // One CTA scans `rows_per_cta` codes for G queries. Shared-memory LUT layout
 // is [sub][code][G]: the G threads that share a code read G consecutive words,
 // so a warp's gathers touch at most 32/G distinct 32-word rows.
-template <int G, int BUF>
+// M > 0: m == M (a multiple of 16) and ksub == 256, so table offsets and
+// code byte positions are compile-time constants; M == 0: any m and ksub.
+template <int G, int BUF, int M>
 __global__ void __launch_bounds__(kPqThreads)
 pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
                const float* __restrict__ lut, int nq, int k, int64_t rows_per_cta,
@@ -92,7 +103,29 @@ pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
     float key[G];
 #pragma unroll
     for (int i = 0; i < G; ++i) key[i] = 0.0f;
-    if (vec16) {
+    if constexpr (M > 0) {
+      const uint32_t lbase = lut_addr + static_cast<uint32_t>(g * 4);
+#pragma unroll
+      for (int b = 0; b < M; b += 16) {
+        uint4 w[G];
+#pragma unroll
+        for (int i = 0; i < G; ++i)
+          w[i] = ok[i] ? __ldg(reinterpret_cast<const uint4*>(codes + rr[i] * M + b)) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+#pragma unroll
+          for (int bi = 0; bi < 4; ++bi) {
+            const uint32_t lsub = lbase + static_cast<uint32_t>((b + wi * 4 + bi) * 256 * G * 4);
+#pragma unroll
+            for (int i = 0; i < G; ++i) {
+              const uint32_t word = wi == 0 ? w[i].x : (wi == 1 ? w[i].y : (wi == 2 ? w[i].z : w[i].w));
+              const uint32_t c = __byte_perm(word, 0u, 0x4440u | static_cast<uint32_t>(bi));
+              key[i] = __fadd_rn(key[i], lds_f32_sched(lsub + c * (G * 4)));
+            }
+          }
+        }
+      }
+    } else if (vec16) {
       for (int b = 0; b < m; b += 16) {
         uint4 w[G];
 #pragma unroll
@@ -140,16 +173,25 @@ pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
   }
 }
 
-template <int G, int BUF>
-cudaError_t launch_pq_g(const PqScanArgs& a, cudaStream_t stream) {
+template <int G, int BUF, int M>
+cudaError_t launch_pq_gm(const PqScanArgs& a, cudaStream_t stream) {
   const size_t smem = pq_smem_for(G, a.m, a.ksub, a.k);
-  auto kern = pq_scan_kernel<G, BUF>;
+  auto kern = pq_scan_kernel<G, BUF, M>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.ncta, (a.nq + G - 1) / G);
   kern<<<grid, kPqThreads, smem, stream>>>(a.codes, a.n, a.m, a.ksub, a.lut, a.nq, a.k,
                                            a.rows_per_cta, a.mask, a.partial);
   return cudaGetLastError();
+}
+
+template <int G, int BUF>
+cudaError_t launch_pq_g(const PqScanArgs& a, cudaStream_t stream) {
+  if (a.ksub == 256) {
+    if (a.m == 16) return launch_pq_gm<G, BUF, 16>(a, stream);
+    if (a.m == 32) return launch_pq_gm<G, BUF, 32>(a, stream);
+  }
+  return launch_pq_gm<G, BUF, 0>(a, stream);
 }
 
 template <int BUF>

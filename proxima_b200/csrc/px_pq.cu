@@ -161,11 +161,23 @@ static px_status pq_shard_search(const px_pq* h, PqShard& sh, const float* d_q, 
   const size_t smem = pq_smem_for(group, h->m, h->ksub, k);
   if (smem > 227 * 1024) return set_error(PX_EUNSUPPORTED, "PQ table too large for shared memory");
   const int per_sm = std::max<int>(1, static_cast<int>((227 * 1024) / smem));
-  const int64_t target = static_cast<int64_t>(sh.sms) * std::min(per_sm, 4) * 2;
+  const int64_t slots = static_cast<int64_t>(sh.sms) * std::min(per_sm, 4);  // co-resident CTAs
   const int64_t n = std::max<int64_t>(sh.n, 1);
-  int64_t ncta = std::max<int64_t>(1, (target + groups - 1) / groups);
-  ncta = std::min<int64_t>(ncta, (n + 511) / 512);
-  ncta = std::min<int64_t>(ncta, 1024);
+  // Row slices per query group: at least two waves of CTAs, and a total that
+  // fills its last wave (a 2.5-wave grid leaves half the GPU idle at the end).
+  const int64_t max_cta = std::max<int64_t>(1, std::min<int64_t>((n + 511) / 512, 1024));
+  const int64_t lo = std::min<int64_t>(max_cta, std::max<int64_t>(1, (2 * slots + groups - 1) / groups));
+  int64_t ncta = lo;
+  double best = 0.0;
+  for (int64_t cand = lo; cand <= std::min<int64_t>(max_cta, 4 * lo); ++cand) {
+    const int64_t total = groups * cand;
+    const double fill = static_cast<double>(total) / (static_cast<double>((total + slots - 1) / slots) * slots);
+    if (fill > best + 1e-9) {
+      best = fill;
+      ncta = cand;
+    }
+    if (fill >= 0.97) break;
+  }
   int64_t rows = (n + ncta - 1) / ncta;
   rows = (rows + 511) / 512 * 512;
   ncta = (n + rows - 1) / rows;
