@@ -63,7 +63,7 @@ template <int QT, int KIND> struct Tile {
   static constexpr int STAGE_BYTES = QT * A_TILE + B_TILE;
   static constexpr int NBARS = 2 * STAGES + 2 + 2 + 1;  // full, empty, tmem full, tmem empty, done
   static constexpr int THREADS = 64 + 128 * QT;  // TMA warp, MMA warp, QT epilogue warpgroups
-  static constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + NBARS * 8 + 16;
+  static constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + NBARS * 8 + 16 + 128 * QT * 33 * 4;
 };
 
 __device__ __forceinline__ bool mbar_wait_quiet(uint32_t bar, uint32_t parity) {
@@ -152,12 +152,31 @@ __device__ __forceinline__ uint32_t low_bits(int n) {
   return n <= 0 ? 0u : (n >= 32 ? 0xffffffffu : (1u << n) - 1u);
 }
 
+// Inserts the columns of `pass` (keys in slot[0..31], rows rbase ..) that
+// beat the running threshold into the top-CAP list.
+template <int CAP>
+__device__ __forceinline__ void insert_passing(uint64_t (&L)[CAP], uint64_t& thr, float& thr_key, int& maxpos,
+                                               uint32_t pass, const float* slot, int64_t rbase) {
+  while (pass) {
+    const int j = __ffs(pass) - 1;
+    pass &= pass - 1;
+    const float kj = slot[j];
+    if (kj <= thr_key) {
+      const uint64_t cand = pack_cand(kj, static_cast<uint32_t>(rbase + j));
+      if (cand < thr) {
+        list_insert<CAP>(L, thr, maxpos, cand);
+        thr_key = thr == PX_EMPTY ? __int_as_float(0x7f800000) : cand_key(thr);
+      }
+    }
+  }
+}
+
 // Drains NCOL accumulator columns (base rows row0 ..) of this thread's TMEM
 // lane into its top-CAP list, 64 columns per step: two TMEM loads in flight
 // and one wait, approximate keys, two independent three-input min trees that
 // reject the 64 columns in the common case, and the exact per-column test and
-// insertion otherwise. taddr: the lane's TMEM address of column 0; slot: 64
-// floats of this thread (local memory), touched only on the rare path.
+// insertion otherwise. taddr: the lane's TMEM address of column 0; slot: 32
+// floats of this thread in shared memory, touched only on the rare path.
 template <int CAP, bool L2, int NCOL>
 __device__ __forceinline__ void drain_columns(uint64_t (&L)[CAP], uint64_t& thr, float& thr_key, int& maxpos,
                                               uint32_t taddr, int64_t row0, int valid_cols,
@@ -197,31 +216,17 @@ __device__ __forceinline__ void drain_columns(uint64_t (&L)[CAP], uint64_t& thr,
       pass0 &= __ldg(p.mask_bits + (rbase >> 5));
       pass1 &= __ldg(p.mask_bits + (rbase >> 5) + 1);
     }
-    if (pass0 | pass1) {
-      // Rare path, one copy of the insertion code: the keys of a half with
-      // a passing column go through this thread's slot so they can be
-      // indexed.
-      if (pass0) {
+    // Rare path: the keys of a half with a passing column go through this
+    // thread's shared-memory slot so they can be indexed.
+    if (pass0) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) slot[j] = k0[j];
-      }
-      if (pass1) {
+      for (int j = 0; j < 32; ++j) slot[j] = k0[j];
+      insert_passing<CAP>(L, thr, thr_key, maxpos, pass0, slot, rbase);
+    }
+    if (pass1) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) slot[32 + j] = k1[j];
-      }
-      uint64_t pass = static_cast<uint64_t>(pass0) | (static_cast<uint64_t>(pass1) << 32);
-      while (pass) {
-        const int j = __ffsll(static_cast<long long>(pass)) - 1;
-        pass &= pass - 1;
-        const float kj = slot[j];
-        if (kj <= thr_key) {
-          const uint64_t cand = pack_cand(kj, static_cast<uint32_t>(rbase + j));
-          if (cand < thr) {
-            list_insert<CAP>(L, thr, maxpos, cand);
-            thr_key = thr == PX_EMPTY ? __int_as_float(0x7f800000) : cand_key(thr);
-          }
-        }
-      }
+      for (int j = 0; j < 32; ++j) slot[j] = k1[j];
+      insert_passing<CAP>(L, thr, thr_key, maxpos, pass1, slot, rbase + 32);
     }
   }
 }
@@ -243,6 +248,7 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + TL::NBARS);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+  float* s_keys = reinterpret_cast<float*>(s_tmem + 4);  // (128 * QT) x 33 epilogue key slots
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -412,7 +418,7 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const int quarter = warp & 3;    // TMEM lanes this warp may access
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-    float slot[64];  // local memory, touched only on the rare insertion path
+    float* slot = s_keys + (wg * 128 + row_in_tile) * 33;
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
@@ -488,9 +494,9 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 //   done      each CTA; every MMA has completed
 // Each CTA's two epilogue warpgroups drain 128 columns each of every tile, so
 // every (query, split) has two lists. The epilogue's rare insertion path
-// indexes its keys through local memory, so shared memory holds only the
-// ring. (A seventh stage, or prefetching base slices into L2 ahead of the
-// ring, measured slower on config 4.)
+// indexes its keys through a 33-float shared-memory slot per thread (local
+// memory spilled to DRAM on config 4's frequent refills). A seventh stage,
+// or prefetching base slices into L2 ahead of the ring, measured slower.
 namespace pairk {
 constexpr int PM = 128;                         // query rows per CTA (TMEM lanes)
 constexpr int PH = 128;                         // base rows staged per CTA
@@ -500,7 +506,7 @@ constexpr int A_TILE = PM * ROW;                // 16 KB
 constexpr int STAGE_BYTES = A_TILE + PH * ROW;  // 32 KB
 constexpr int NBARS = 2 * STAGES + 2 + 2 + 1;
 constexpr int THREADS = 64 + 256;
-constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + NBARS * 8 + 16;
+constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + NBARS * 8 + 16 + 256 * 33 * 4;
 }  // namespace pairk
 
 // Largest k the bf16 pass serves (its candidates then number 256, the most
@@ -518,6 +524,7 @@ gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NBARS);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+  float* s_keys = reinterpret_cast<float*>(s_tmem + 4);  // 256 x 33 epilogue key slots
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -665,7 +672,7 @@ gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     const int quarter = warp & 3;      // TMEM lanes this warp may access
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-    float slot[64];  // local memory, touched only on the rare insertion path
+    float* slot = s_keys + (half * 128 + row_in_tile) * 33;
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
