@@ -407,3 +407,33 @@ def test_tensor_path_three_tiers(pxm, metric):
     ids, d, prof = _run_path(pxm, data, metric, queries[:20], 10, "tensor")
     _parity.check_flat(data, metric, queries[:20], ids, d, 10)
     assert prof["refined_queries"] == 0 and prof["fallback_queries"] > 0, prof
+
+
+@pytest.mark.parametrize("metric", [O.L2, O.IP])
+@pytest.mark.parametrize("n,nq,k", [(100, 300, 10), (257, 64, 16), (513, 257, 40), (1000, 513, 100)])
+def test_tensor_path_tile_edges(pxm, metric, n, nq, k):
+    # Shards shorter than one 256-row pair tile or one row past a tile, and
+    # query counts one past a 256-query group: the tiles' tails, the padded
+    # query rows and the (few) split lists all stay exact.
+    dim = 64
+    data = _data.unit_gaussian(n, dim, n + 11)
+    queries = _data.unit_gaussian(nq, dim, nq + 13)
+    ids, d, prof = _run_path(pxm, data, metric, queries, k, "tensor")
+    assert prof["path"] == "tensor" and prof["first_pass"] == "bf16"
+    _parity.check_flat(data, metric, queries, ids, d, k)
+
+
+@pytest.mark.parametrize("metric", [O.L2, O.IP])
+def test_tensor_path_filtered_large_k(pxm, metric):
+    # k = 100 on the bf16 pass (32-candidate lists, 256 rescored) with filters.
+    n, dim, nq, k = 30000, 96, 64, 100
+    data = _data.unit_gaussian(n, dim, 41)
+    queries = _data.unit_gaussian(nq, dim, 42)
+    idx = pxm.FlatIndex(dim, _metric(pxm, metric))
+    idx.add(data)
+    idx.set_search_path("tensor")
+    rng = np.random.default_rng(43)
+    for mask in (rng.random(n) < 0.5, np.arange(n) % 7 == 0, np.arange(n) < 150):
+        ids, d = idx.search_batch_filtered(queries, mask, k=k)
+        assert idx.last_search_profile()["first_pass"] == "bf16"
+        _parity.check_flat(data, metric, queries, ids, d, k, filter_=mask)
