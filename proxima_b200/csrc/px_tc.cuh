@@ -240,9 +240,13 @@ __device__ __forceinline__ void fence_mbarrier_init_cluster() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
-// Arrive on an mbarrier given by its shared::cluster address (this or the peer CTA).
+// Arrive on an mbarrier given by its shared::cluster address (this or the
+// peer CTA), with the instruction's default semantics (release, CTA scope):
+// what it publishes is the completion of this thread's tcgen05.ld reads,
+// ordered before it by tcgen05.fence::before_thread_sync, not memory writes
+// the peer reads, so no cluster-wide memory barrier is needed.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 
 // 2-D tiled TMA load (no multicast) into this CTA's shared memory whose
