@@ -297,6 +297,8 @@ px_status FlatShard::append_device(const float* d_src, int64_t count, int d, int
   return PX_OK;
 }
 
+static void clear_flat_graphs(px_flat* h);
+
 static px_status flat_check(const px_flat* h) {
   if (h == nullptr) return set_error(PX_EINVAL, "null handle");
   return PX_OK;
@@ -358,6 +360,7 @@ PX_API px_status px_flat_destroy(px_flat* h) {
   if (h == nullptr) return PX_OK;
   {
     std::lock_guard<std::mutex> lk(h->mu);
+    clear_flat_graphs(h);
     for (auto& sh : h->shards) sh.release();
     h->gather.release_all();
     h->pinned.release();
@@ -425,6 +428,7 @@ PX_API px_status px_flat_add(px_flat* h, const float* rows, int64_t n) {
   if (!all_finite(rows, n * h->dim))
     return set_error(PX_EINVAL, "vectors must not contain NaN or infinite values");
   std::lock_guard<std::mutex> lk(h->mu);
+  clear_flat_graphs(h);  // the rows they read may move
   const int G = static_cast<int>(h->shards.size());
   std::vector<int64_t> begin, count;
   split_rows(n, G, begin, count);
@@ -476,6 +480,7 @@ PX_API px_status px_flat_reserve(px_flat* h, int64_t n_total) {
   if (s != PX_OK) return s;
   if (n_total < 0) return set_error(PX_EINVAL, "row count must be >= 0");
   std::lock_guard<std::mutex> lk(h->mu);
+  clear_flat_graphs(h);  // the rows they read may move
   const int64_t G = static_cast<int64_t>(h->shards.size());
   const int64_t per = (n_total + G - 1) / G;
   for (auto& sh : h->shards) {
@@ -494,6 +499,7 @@ PX_API px_status px_flat_add_device(px_flat* h, const float* d_rows, int64_t n) 
   if (n < 0) return set_error(PX_EINVAL, "row count must be >= 0");
   if (n == 0) return PX_OK;
   std::lock_guard<std::mutex> lk(h->mu);
+  clear_flat_graphs(h);  // the rows they read may move
   FlatShard& sh = h->shards[0];
   if (sh.n + n > 0xFFFFFFFFll) return set_error(PX_EUNSUPPORTED, "a shard holds at most 2^32-1 rows");
   DeviceGuard dg(sh.device);
@@ -528,6 +534,139 @@ static px_status shard_search(const px_flat* h, FlatShard& sh, int metric, const
   return PX_OK;
 }
 
+// Small batches on a single-shard handle, when the plan is the exact scan (no
+// host wait inside the search): the upload, scan, merge, emit and download
+// are captured once as a CUDA graph and replayed, which replaces five
+// launches and copies by one graph launch. Each graph owns its page-locked
+// staging and its device buffers; besides those it reads only the shard's
+// rows and segment table, and every call that can reallocate those first
+// destroys the handle's graphs (clear_flat_graphs).
+static constexpr size_t kMaxFlatGraphs = 8;
+
+static void destroy_flat_graph(FlatSearchGraph& g) {
+  if (g.exec) cudaGraphExecDestroy(g.exec);
+  if (g.dev) cudaFree(g.dev);
+  if (g.pinned) cudaFreeHost(g.pinned);
+  g.exec = nullptr;
+  g.dev = nullptr;
+  g.pinned = nullptr;
+}
+
+static void clear_flat_graphs(px_flat* h) {
+  if (h->graphs.empty()) return;
+  DeviceGuard dg(h->shards[0].device);
+  cudaStreamSynchronize(h->shards[0].stream);
+  for (auto& g : h->graphs) destroy_flat_graph(g);
+  h->graphs.clear();
+}
+
+// Sets *captured = false (and returns PX_OK) when the graph cannot be built,
+// so the caller runs the search without one.
+static px_status flat_search_replay(px_flat* h, FlatShard& sh, const SearchPlan& plan_in, int metric,
+                                    const float* queries, int64_t nq, int32_t k, bool natural, int64_t* out_ids,
+                                    float* out_dists, bool* captured) {
+  *captured = true;
+  SearchPlan plan = plan_in;
+  const size_t qbytes = sizeof(float) * static_cast<size_t>(nq) * h->dim;
+  const size_t obytes = static_cast<size_t>(nq) * k;
+  const size_t q_al = (qbytes + 15) & ~size_t(15);
+  FlatSearchGraph key;
+  key.nq = nq;
+  key.n = sh.n;
+  key.id_offset = h->id_offset;
+  key.rows_per_cta = plan.rows_per_cta;
+  key.k = k;
+  key.metric = metric;
+  key.natural = natural ? 1 : 0;
+  key.group = plan.group;
+  key.ncta = plan.ncta;
+  auto same = [&](const FlatSearchGraph& g) {
+    return g.nq == key.nq && g.n == key.n && g.id_offset == key.id_offset && g.rows_per_cta == key.rows_per_cta &&
+           g.k == key.k && g.metric == key.metric && g.natural == key.natural && g.group == key.group &&
+           g.ncta == key.ncta;
+  };
+  FlatSearchGraph* hit = nullptr;
+  for (auto& g : h->graphs)
+    if (same(g)) hit = &g;
+
+  if (hit == nullptr) {
+    // Buffers for this graph alone: [queries | ids | dists] page-locked, and
+    // [queries | ids | dists | workspace] on the device.
+    Carver c;
+    c.take(qbytes);
+    c.take(obytes * sizeof(int64_t));
+    c.take(obytes * sizeof(float));
+    void* ws_at = c.take(plan.ws_bytes);
+    (void)ws_at;
+    if (cudaMallocHost(&key.pinned, q_al + obytes * 12 + 16) != cudaSuccess ||
+        cudaMalloc(&key.dev, c.used) != cudaSuccess) {
+      cudaGetLastError();
+      destroy_flat_graph(key);
+      *captured = false;
+      return PX_OK;
+    }
+    c = Carver{key.dev};
+    float* d_q = static_cast<float*>(c.take(qbytes));
+    int64_t* d_ids = static_cast<int64_t*>(c.take(obytes * sizeof(int64_t)));
+    float* d_d = static_cast<float*>(c.take(obytes * sizeof(float)));
+    void* d_ws = c.take(plan.ws_bytes);
+    char* pin = static_cast<char*>(key.pinned);
+    const int64_t launches0 = g_launches.load();
+    cudaGraph_t graph = nullptr;
+    cudaError_t ce = cudaStreamBeginCapture(sh.stream, cudaStreamCaptureModeThreadLocal);
+    px_status ps = PX_OK;
+    if (ce == cudaSuccess) {
+      ce = cudaMemcpyAsync(d_q, pin, qbytes, cudaMemcpyHostToDevice, sh.stream);
+      if (ce == cudaSuccess) ps = run_flat_search(h, sh, plan, metric, d_q, nq, k, nullptr, sh.stream, d_ws);
+      if (ps == PX_OK && ce == cudaSuccess)
+        ce = launch_emit(plan.final_cands, nq, k, metric == PX_METRIC_L2, natural, sh.segs.view(h->id_offset),
+                         d_ids, d_d, sh.stream);
+      if (ps == PX_OK && ce == cudaSuccess)
+        ce = cudaMemcpyAsync(pin + q_al, d_ids, obytes * sizeof(int64_t), cudaMemcpyDeviceToHost, sh.stream);
+      if (ps == PX_OK && ce == cudaSuccess)
+        ce = cudaMemcpyAsync(pin + q_al + obytes * sizeof(int64_t), d_d, obytes * sizeof(float),
+                             cudaMemcpyDeviceToHost, sh.stream);
+      const cudaError_t ee = cudaStreamEndCapture(sh.stream, &graph);
+      if (ce == cudaSuccess) ce = ee;
+    }
+    g_launches.fetch_sub(g_launches.load() - launches0);  // counted when replayed
+    if (ps == PX_OK && ce == cudaSuccess) ce = cudaGraphInstantiate(&key.exec, graph, 0);
+    if (graph) cudaGraphDestroy(graph);
+    if (ps != PX_OK || ce != cudaSuccess) {
+      cudaGetLastError();
+      destroy_flat_graph(key);
+      *captured = false;
+      return PX_OK;
+    }
+    if (h->graphs.size() >= kMaxFlatGraphs) {
+      auto oldest = h->graphs.begin();
+      for (auto it = h->graphs.begin(); it != h->graphs.end(); ++it)
+        if (it->last_use < oldest->last_use) oldest = it;
+      destroy_flat_graph(*oldest);
+      h->graphs.erase(oldest);
+    }
+    h->graphs.push_back(key);
+    hit = &h->graphs.back();
+  }
+  hit->last_use = ++h->graph_clock;
+  char* pin = static_cast<char*>(hit->pinned);
+  std::memcpy(pin, queries, qbytes);
+  cudaError_t e = cudaGraphLaunch(hit->exec, sh.stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(sh.stream);
+  if (e != cudaSuccess) return cuda_status(e, "search");
+  // The replayed kernels: the exact scan, its merge, and the emit.
+  g_launches += 3;
+  sh.last_path = static_cast<int>(FlatPath::Exact);
+  sh.last_fallback = 0;
+  sh.last_refined = 0;
+  sh.last_pass = -1;
+  sh.last_launches = 3;
+  sh.last_profiled = false;
+  std::memcpy(out_ids, pin + q_al, obytes * sizeof(int64_t));
+  std::memcpy(out_dists, pin + q_al + obytes * sizeof(int64_t), obytes * sizeof(float));
+  return PX_OK;
+}
+
 // Full host-to-host search over every shard.
 static px_status flat_search_host(const px_flat* hc, int metric, const float* queries, int64_t nq,
                                   int32_t k, const uint8_t* mask, bool natural, int64_t* out_ids,
@@ -538,6 +677,21 @@ static px_status flat_search_host(const px_flat* hc, int metric, const float* qu
   const size_t qbytes = sizeof(float) * static_cast<size_t>(nq) * h->dim;
   const size_t obytes = static_cast<size_t>(nq) * k;
   std::vector<uint8_t> local_mask;
+
+  if (G == 1 && mask == nullptr && g_profiling.load() == 0) {
+    FlatShard& sh = h->shards[0];
+    DeviceGuard dg(sh.device);
+    px_status s = sh.segs.sync_device();
+    if (s != PX_OK) return s;
+    SearchPlan plan;
+    s = plan_flat_search(h, sh, nq, k, false, plan);
+    if (s != PX_OK) return s;
+    if (plan.path == FlatPath::Exact) {
+      bool captured = false;
+      s = flat_search_replay(h, sh, plan, metric, queries, nq, k, natural, out_ids, out_dists, &captured);
+      if (s != PX_OK || captured) return s;
+    }
+  }
 
   // Host buffers that are not page-locked go through a pinned staging buffer
   // of the handle, so the copies are asynchronous DMA transfers.

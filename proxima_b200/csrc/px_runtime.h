@@ -126,6 +126,19 @@ struct GatherBuf {
   void release_all();
 };
 
+// A captured small-batch search (query upload, exact scan, merge, emit,
+// result download) with the staging and workspace buffers it owns. Besides
+// those it depends only on the shard's rows and segment table, which change
+// only through an add or reserve; those clear the handle's graphs first.
+struct FlatSearchGraph {
+  int64_t nq = 0, n = 0, id_offset = 0, rows_per_cta = 0;
+  int k = 0, metric = 0, natural = 0, group = 0, ncta = 0;
+  cudaGraphExec_t exec = nullptr;
+  void* pinned = nullptr;  // page-locked queries and results (owned)
+  void* dev = nullptr;     // device queries, results and scan workspace (owned)
+  uint64_t last_use = 0;
+};
+
 struct px_flat {
   int dim = 0;
   int ld = 0;   // fp32 / split-plane row stride: dim rounded up to 32
@@ -137,6 +150,8 @@ struct px_flat {
   std::vector<FlatShard> shards;
   GatherBuf gather;
   px::HostBuf pinned;  // staging for pageable host buffers
+  std::vector<FlatSearchGraph> graphs;  // single-shard small-batch replays (shard 0's device)
+  uint64_t graph_clock = 0;
   std::mutex mu;
 };
 
@@ -166,6 +181,6 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
                            SearchPlan& plan);
 px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int metric,
                           const float* d_q, int64_t nq, int k, const uint8_t* d_mask,
-                          cudaStream_t stream);
+                          cudaStream_t stream, void* ws = nullptr);
 
 }  // namespace px

@@ -301,7 +301,7 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
 
 px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int metric,
                           const float* d_q, int64_t nq, int k, const uint8_t* d_mask,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, void* ws) {
   const bool prof = g_profiling.load() != 0;
   sh.last_path = static_cast<int>(plan.path);
   sh.last_fallback = 0;
@@ -309,7 +309,7 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   sh.last_pass = -1;
   sh.last_profiled = prof;
   const int64_t launches0 = g_launches.load();
-  Carver c(sh.ws.ptr);
+  Carver c(ws ? ws : sh.ws.ptr);
   if (plan.path == FlatPath::Exact) {
     plan.partial = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.ncta * k));
     plan.final_cands = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * k));

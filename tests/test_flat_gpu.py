@@ -437,3 +437,31 @@ def test_tensor_path_filtered_large_k(pxm, metric):
         ids, d = idx.search_batch_filtered(queries, mask, k=k)
         assert idx.last_search_profile()["first_pass"] == "bf16"
         _parity.check_flat(data, metric, queries, ids, d, k, filter_=mask)
+
+
+def test_small_batch_graph_replay(pxm):
+    # Small batches on one device run as a replayed CUDA graph: new query
+    # values, alternating shapes and k (several cached graphs), an add that
+    # grows the index (the graph must be rebuilt) and the launch count.
+    from proxima_b200 import _lib
+    dim = 48
+    data = _data.unit_gaussian(6000, dim, 71)
+    idx = pxm.FlatIndex(dim, pxm.Metric.L2)
+    idx.add(data[:4000])
+    rng = np.random.default_rng(72)
+    for step in range(6):
+        nq, k = ((1, 10), (3, 5), (1, 10), (7, 32))[step % 4]
+        q = rng.standard_normal((nq, dim)).astype(np.float32)
+        before = _lib.launch_count()
+        ids, d = idx.search_batch(q, k=k)
+        assert idx.last_search_profile()["path"] == "exact"
+        assert _lib.launch_count() - before == 3
+        _parity.check_flat(data[:4000], O.L2, q, ids, d, k)
+    idx.add(data[4000:])
+    for _ in range(3):
+        q = rng.standard_normal((1, dim)).astype(np.float32)
+        ids, d = idx.search(q[0], k=10)
+        _parity.check_flat(data, O.L2, q, ids[None, :], d[None, :], 10)
+    # A query equal to a base row finds it at distance 0 in the grown index.
+    ids, d = idx.search(data[4321], k=3)
+    assert ids[0] == 4321 and d[0] == 0.0
