@@ -68,7 +68,7 @@ exact_scan_kernel(const float* __restrict__ base, int64_t n, int ld, int d,
     if (valid) {
       const float* xrow = base + r * ld + half * 4;
       const float* qh = s_q + half * 4;
-#pragma unroll 4
+#pragma unroll 8  // eight 16-byte loads in flight per thread
       for (int c = 0; c < chunks; ++c) {
         float4 x = ldg_stream4(xrow + c * 8);
 #pragma unroll
