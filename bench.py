@@ -214,13 +214,13 @@ def cpu_threads():
     return host_cores()
 
 
-def cpu_sample_qps(base_host, metric, queries_host, k, sample):
+def cpu_sample_qps(base_host, metric, queries_host, k, sample, threads=None):
     """Times the oracle (reference CPU path restated) on `sample` queries."""
     import oracle as O
     m = O.L2 if metric == "l2" else O.IP
     q = np.ascontiguousarray(queries_host[:sample])
     t = time.perf_counter()
-    ids, d = O.flat_search_batch(base_host, m, q, k, num_threads=host_cores())
+    ids, d = O.flat_search_batch(base_host, m, q, k, num_threads=threads or host_cores())
     dt = time.perf_counter() - t
     return sample / dt, dt, ids, d
 
@@ -328,9 +328,15 @@ def run_pq(args, cfg, rank, world, local_rank):
         t = time.perf_counter()
         ref_ids, ref_d = O.pq_search_batch(books, O.L2, codes, queries[:sample], k, num_threads=host_cores())
         dt = time.perf_counter() - t
+        s1 = max(1, sample // cpu_threads())
+        t1 = time.perf_counter()
+        O.pq_search_batch(books, O.L2, codes, queries[:s1], k, num_threads=1)
+        dt1 = time.perf_counter() - t1
         cpu = {"value": sample / dt, "unit": "queries/s", "cores": cpu_threads(), "kind": "port",
                "sample": f"first {sample} of the {nq} queries against all {n} codes ({dt:.2f} s); "
-                         "C++ restatement of PqIndex::search_batch, all host threads"}
+                         "C++ restatement of PqIndex::search_batch, all host threads",
+               "single_thread": {"value": s1 / dt1, "unit": "queries/s", "cores": 1,
+                                 "sample": f"first {s1} queries, one thread ({dt1:.2f} s)"}}
         try:
             ties = _parity.check(ids[:sample], d[:sample], ref_ids, ref_d,
                                  _parity.pq_natural(books, O.L2, codes, queries[:sample]))
@@ -509,9 +515,14 @@ def run_ours(args, cfg, rank, world, local_rank):
         qh = queries.cpu().numpy()
         sample = args.cpu_sample
         qps, dt, ref_ids, ref_d = cpu_sample_qps(base_host, metric, qh, k, sample)
+        # The same path on one thread, on a proportionally smaller sample.
+        s1 = max(1, sample // cpu_threads())
+        qps1, dt1, _, _ = cpu_sample_qps(base_host, metric, qh, k, s1, threads=1)
         cpu = {"value": qps, "unit": "queries/s", "cores": cpu_threads(), "kind": "port",
                "sample": f"first {sample} of the {nq} queries against the full {n}x{dim} base "
-                         f"({dt:.1f} s); C++ restatement of FlatIndex::search_batch, all host threads"}
+                         f"({dt:.1f} s); C++ restatement of FlatIndex::search_batch, all host threads",
+               "single_thread": {"value": qps1, "unit": "queries/s", "cores": 1,
+                                 "sample": f"first {s1} queries, one thread ({dt1:.1f} s)"}}
         import oracle as O
         from tests import _parity
         ids, d = index.search_device(queries[:sample].contiguous(), k)
