@@ -77,6 +77,25 @@ __device__ __forceinline__ float min3f(float a, float b, float c) {
   return r;
 }
 
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Largest of 32 raw accumulator words (as floats), the same tree with max.
+__device__ __forceinline__ float max32u(const uint32_t (&v)[32]) {
+  float a[10];
+#pragma unroll
+  for (int i = 0; i < 10; ++i)
+    a[i] = max3f(__uint_as_float(v[3 * i]), __uint_as_float(v[3 * i + 1]), __uint_as_float(v[3 * i + 2]));
+  const float b0 = max3f(a[0], a[1], a[2]);
+  const float b1 = max3f(a[3], a[4], a[5]);
+  const float b2 = max3f(a[6], a[7], a[8]);
+  const float b3 = max3f(a[9], __uint_as_float(v[30]), __uint_as_float(v[31]));
+  return fmaxf(max3f(b0, b1, b2), b3);
+}
+
 // Smallest of 32 keys: a depth-4 tree of three-input minimums (16 ops).
 __device__ __forceinline__ float min32(const float (&k)[32]) {
   float a[10];
@@ -192,15 +211,26 @@ __device__ __forceinline__ void drain_columns(uint64_t (&L)[CAP], uint64_t& thr,
     const int64_t rbase = row0 + c * 64;
     const int nvalid = valid_cols - c * 64;
     if (nvalid <= 0) continue;
+    const bool whole = nvalid >= 64 && p.mask_bits == nullptr;
+    float m0, m1;
+    if (!L2) {
+      // Inner product: the keys are -v, and -max(v) == min(-v) exactly, so
+      // the common case needs no negated keys at all.
+      m0 = -max32u(v0);
+      m1 = -max32u(v1);
+      if (whole && !(fminf(m0, m1) <= thr_key)) continue;
+    }
     float k0[32], k1[32];
     chunk_keys<L2>(v0, p, rbase, k0);
     chunk_keys<L2>(v1, p, rbase + 32, k1);
     // Common case: nothing in the 64 columns beats the threshold. Partial or
     // filtered steps take the exact per-column test; otherwise only a half
     // whose minimum can pass does.
-    const float m0 = min32(k0), m1 = min32(k1);
-    const bool whole = nvalid >= 64 && p.mask_bits == nullptr;
-    if (whole && !(fminf(m0, m1) <= thr_key)) continue;
+    if (L2) {
+      m0 = min32(k0);
+      m1 = min32(k1);
+      if (whole && !(fminf(m0, m1) <= thr_key)) continue;
+    }
     uint32_t pass0 = 0, pass1 = 0;
     if (!whole || m0 <= thr_key) {
 #pragma unroll
