@@ -36,6 +36,14 @@ __device__ __forceinline__ float lds_f32_sched(uint32_t addr) {
   return v;
 }
 
+// Four adjacent table entries (one code, four queries) in one 16-byte load;
+// same scheduling freedom and the same condition on the address.
+__device__ __forceinline__ float4 lds_f32x4_sched(uint32_t addr) {
+  float4 v;
+  asm("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+
 __global__ void pq_lut_kernel(const float* __restrict__ books, int m, int ksub, int dsub, bool l2,
                               const float* __restrict__ queries, float* __restrict__ lut) {
   const int q = blockIdx.x;
@@ -88,6 +96,67 @@ pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
   const uint32_t lut_addr = static_cast<uint32_t>(__cvta_generic_to_shared(s_lut));
   uint64_t thr = PX_EMPTY;
 
+  if constexpr (M > 0 && G == 8) {
+    // Two threads per row, each serving four of the eight queries: the
+    // table's [sub][code][8] layout puts a code's four entries side by side,
+    // so one 16-byte load feeds four sequential per-query sums. Each thread
+    // takes kQuadRows rows per iteration (independent chains).
+    constexpr int kQuadRows = kPqRowsPerIter / (kPqThreads / 2);
+    const int quad = tid & 1;
+    const int qslot = tid >> 1;  // 0 .. kPqThreads/2 - 1
+    const uint32_t qbase = lut_addr + static_cast<uint32_t>(quad * 16);
+    uint64_t thr4[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) thr4[j] = PX_EMPTY;
+    for (int64_t it = row_begin; it < row_end; it += kPqRowsPerIter) {
+      bool ok[kQuadRows];
+      int64_t rr[kQuadRows];
+#pragma unroll
+      for (int r = 0; r < kQuadRows; ++r) {
+        rr[r] = it + r * (kPqThreads / 2) + qslot;
+        ok[r] = rr[r] < row_end && (mask == nullptr || mask[rr[r]] != 0);
+      }
+      float key[kQuadRows][4];
+#pragma unroll
+      for (int r = 0; r < kQuadRows; ++r)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) key[r][j] = 0.0f;
+#pragma unroll
+      for (int b = 0; b < M; b += 16) {
+        uint4 w[kQuadRows];
+#pragma unroll
+        for (int r = 0; r < kQuadRows; ++r)
+          w[r] = ok[r] ? __ldg(reinterpret_cast<const uint4*>(codes + rr[r] * M + b)) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+#pragma unroll
+          for (int bi = 0; bi < 4; ++bi) {
+            const uint32_t lsub = qbase + static_cast<uint32_t>((b + wi * 4 + bi) * 256 * 8 * 4);
+#pragma unroll
+            for (int r = 0; r < kQuadRows; ++r) {
+              const uint32_t word = wi == 0 ? w[r].x : (wi == 1 ? w[r].y : (wi == 2 ? w[r].z : w[r].w));
+              const uint32_t c = __byte_perm(word, 0u, 0x4440u | static_cast<uint32_t>(bi));
+              const float4 t = lds_f32x4_sched(lsub + c * 32);
+              key[r][0] = __fadd_rn(key[r][0], t.x);
+              key[r][1] = __fadd_rn(key[r][1], t.y);
+              key[r][2] = __fadd_rn(key[r][2], t.z);
+              key[r][3] = __fadd_rn(key[r][3], t.w);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kQuadRows; ++r)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (ok[r] && quad * 4 + j < gcount)
+            topk.offer(quad * 4 + j, pack_cand(key[r][j], static_cast<uint32_t>(rr[r])), thr4[j]);
+      __syncthreads();
+      topk.maybe_compact(k, kPqRowsPerIter, tid, kPqThreads);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) thr4[j] = s_thr[quad * 4 + j];
+    }
+  } else
   for (int64_t it = row_begin; it < row_end; it += kPqRowsPerIter) {
     // Each thread scores G rows per iteration for its query g. The G rows'
     // codes are loaded first and their m-long addition chains interleaved
