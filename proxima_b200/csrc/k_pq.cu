@@ -81,9 +81,20 @@ pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
 
   BlockTopK<G, BUF> topk;
   topk.init(s_buf, s_cnt, s_thr, tid, kPqThreads);
-  for (int i = tid; i < G * table; i += kPqThreads) {
-    const int e = i / G, g = i - e * G;
-    s_lut[i] = g < gcount ? lut[static_cast<int64_t>(q0 + g) * table + e] : 0.f;
+  constexpr bool kSkewed = M == 16 && G == 8;
+  if constexpr (kSkewed) {
+    // [sub/8][code][sub%8][query]: a code's entries for eight subs and eight
+    // queries fill 256 bytes, so sub s's 32 bytes sit in bank slice s % 4
+    // whatever the code.
+    for (int d = tid; d < G * table; d += kPqThreads) {
+      const int g = d & 7, s = ((d >> 14) << 3) | ((d >> 3) & 7), c = (d >> 6) & 255;
+      s_lut[d] = g < gcount ? lut[static_cast<int64_t>(q0 + g) * table + s * 256 + c] : 0.f;
+    }
+  } else {
+    for (int i = tid; i < G * table; i += kPqThreads) {
+      const int e = i / G, g = i - e * G;
+      s_lut[i] = g < gcount ? lut[static_cast<int64_t>(q0 + g) * table + e] : 0.f;
+    }
   }
   __syncthreads();
 
@@ -96,61 +107,85 @@ pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
   const uint32_t lut_addr = static_cast<uint32_t>(__cvta_generic_to_shared(s_lut));
   uint64_t thr = PX_EMPTY;
 
-  if constexpr (M > 0 && G == 8) {
-    // Two threads per row, each serving four of the eight queries: the
-    // table's [sub][code][8] layout puts a code's four entries side by side,
-    // so one 16-byte load feeds four sequential per-query sums. Each thread
-    // takes kQuadRows rows per iteration (independent chains).
-    constexpr int kQuadRows = kPqRowsPerIter / (kPqThreads / 2);
+  if constexpr (kSkewed) {
+    // Two threads per row, each serving four of the eight queries with one
+    // 16-byte load per sub. A 16-byte shared load is served a quarter-warp
+    // (four rows) at a time, and four random codes would collide in the four
+    // 32-byte bank slices. So the four rows of a quarter-warp run skewed: the
+    // row at position p is p steps behind, reading sub (i - p) % 16 at step
+    // i, which is bank slice (i - p) % 4 -- four distinct slices, one
+    // wavefront. Each thread streams its kRows rows' codes back to back; every
+    // row still adds its subs in order 0..15 from 0.0, so keys are bit-exact.
+    constexpr int kRows = kPqRowsPerIter / (kPqThreads / 2);
+    constexpr int kWords = M * kRows / 4;  // code words of a thread's rows
+    constexpr int kSkew = 3;
+    constexpr int kSteps = M * kRows + kSkew;
     const int quad = tid & 1;
     const int qslot = tid >> 1;  // 0 .. kPqThreads/2 - 1
-    const uint32_t qbase = lut_addr + static_cast<uint32_t>(quad * 16);
+    const int p = qslot & 3;     // row position within the quarter-warp
+    // off[t]: address of sub (t - p) % 16 for this thread's four queries.
+    uint32_t off[M];
+#pragma unroll
+    for (int t = 0; t < M; ++t) {
+      const int s = (t - p) & (M - 1);
+      off[t] = lut_addr + static_cast<uint32_t>(quad * 16 + (s >> 3) * 65536 + (s & 7) * 32);
+    }
+    const uint32_t shift = 32u - 8u * static_cast<uint32_t>(p);
     uint64_t thr4[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) thr4[j] = PX_EMPTY;
     for (int64_t it = row_begin; it < row_end; it += kPqRowsPerIter) {
-      bool ok[kQuadRows];
-      int64_t rr[kQuadRows];
+      bool ok[kRows];
+      int64_t rr[kRows];
+      uint32_t cw[kWords + 2];  // cw[1 + w] = code word w; zero on both sides
+      cw[0] = 0u;
+      cw[kWords + 1] = 0u;
 #pragma unroll
-      for (int r = 0; r < kQuadRows; ++r) {
+      for (int r = 0; r < kRows; ++r) {
         rr[r] = it + r * (kPqThreads / 2) + qslot;
         ok[r] = rr[r] < row_end && (mask == nullptr || mask[rr[r]] != 0);
+        const uint4 v = ok[r] ? __ldg(reinterpret_cast<const uint4*>(codes + rr[r] * M)) : make_uint4(0, 0, 0, 0);
+        cw[1 + r * 4] = v.x;
+        cw[2 + r * 4] = v.y;
+        cw[3 + r * 4] = v.z;
+        cw[4 + r * 4] = v.w;
       }
-      float key[kQuadRows][4];
+      // The code stream delayed by p bytes: byte i of sw is code byte i - p.
+      uint32_t sw[kWords + 1];
 #pragma unroll
-      for (int r = 0; r < kQuadRows; ++r)
+      for (int w = 0; w <= kWords; ++w) sw[w] = __funnelshift_rc(cw[w], cw[w + 1], shift);
+      float key[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      float fin[kRows][4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) key[r][j] = 0.0f;
+      for (int i = 0; i < kSteps; ++i) {
+        // code << 8 is the code's offset: 256 bytes per code.
+        const uint32_t c8 = __byte_perm(sw[i >> 2], 0u, 0x4404u | (static_cast<uint32_t>(i & 3) << 4));
+        const float4 t = lds_f32x4_sched(off[i & (M - 1)] + c8);
+        if (i >= kSkew || i >= p) {  // before step p this thread's first row has not begun
+          key[0] = __fadd_rn(key[0], t.x);
+          key[1] = __fadd_rn(key[1], t.y);
+          key[2] = __fadd_rn(key[2], t.z);
+          key[3] = __fadd_rn(key[3], t.w);
+        }
 #pragma unroll
-      for (int b = 0; b < M; b += 16) {
-        uint4 w[kQuadRows];
+        for (int r = 0; r < kRows; ++r) {
+          constexpr int kLast = M - 1;
+          const int q = i - r * M - kLast;  // the position whose row r ends at step i
+          if (q >= 0 && q <= kSkew && p == q) {
 #pragma unroll
-        for (int r = 0; r < kQuadRows; ++r)
-          w[r] = ok[r] ? __ldg(reinterpret_cast<const uint4*>(codes + rr[r] * M + b)) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-#pragma unroll
-          for (int bi = 0; bi < 4; ++bi) {
-            const uint32_t lsub = qbase + static_cast<uint32_t>((b + wi * 4 + bi) * 256 * 8 * 4);
-#pragma unroll
-            for (int r = 0; r < kQuadRows; ++r) {
-              const uint32_t word = wi == 0 ? w[r].x : (wi == 1 ? w[r].y : (wi == 2 ? w[r].z : w[r].w));
-              const uint32_t c = __byte_perm(word, 0u, 0x4440u | static_cast<uint32_t>(bi));
-              const float4 t = lds_f32x4_sched(lsub + c * 32);
-              key[r][0] = __fadd_rn(key[r][0], t.x);
-              key[r][1] = __fadd_rn(key[r][1], t.y);
-              key[r][2] = __fadd_rn(key[r][2], t.z);
-              key[r][3] = __fadd_rn(key[r][3], t.w);
+            for (int j = 0; j < 4; ++j) {
+              fin[r][j] = key[j];
+              key[j] = 0.0f;
             }
           }
         }
       }
 #pragma unroll
-      for (int r = 0; r < kQuadRows; ++r)
+      for (int r = 0; r < kRows; ++r)
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           if (ok[r] && quad * 4 + j < gcount)
-            topk.offer(quad * 4 + j, pack_cand(key[r][j], static_cast<uint32_t>(rr[r])), thr4[j]);
+            topk.offer(quad * 4 + j, pack_cand(fin[r][j], static_cast<uint32_t>(rr[r])), thr4[j]);
       __syncthreads();
       topk.maybe_compact(k, kPqRowsPerIter, tid, kPqThreads);
 #pragma unroll

@@ -78,6 +78,30 @@ def test_config3_shape(pxm):
     assert ids1.tolist() == ids[3].tolist()
 
 
+@pytest.mark.parametrize("metric", [O.L2, O.IP])
+def test_m16_scan_edges(pxm, metric):
+    # m = 16 with 256 centroids and 8-query groups is the scan's skewed path:
+    # a ragged row count over several CTAs and iterations, a partial last
+    # group, a filter, and an all-zero query (inner-product entries -0.0,
+    # whose sums must still start from +0.0).
+    rng = np.random.default_rng(16)
+    data = rng.standard_normal((3000, 32)).astype(np.float32)
+    pq = pxm.PqIndex(32, _metric(pxm, metric), m=16, train_iters=4, seed=5)
+    pq.train(data)
+    books = pq.codebooks
+    codes = rng.integers(0, 256, size=(70001, 16), dtype=np.uint8)
+    codes[:40] = codes[40]  # a run of identical rows (exact key ties)
+    pq.add_codes(codes)
+    queries = rng.standard_normal((21, 32)).astype(np.float32)
+    queries[4] = 0.0
+    for k in (1, 10, 50):
+        ids, d = pq.search_batch(queries, k=k)
+        _parity.check_pq(books, metric, codes, queries, ids, d, k)
+    mask = rng.random(len(codes)) < 0.3
+    ids, d = pq.search_batch_filtered(queries, mask, k=10)
+    _parity.check_pq(books, metric, codes, queries, ids, d, 10, filter_=mask)
+
+
 def test_add_codes_and_filters(pxm):
     rng = np.random.default_rng(4)
     data = rng.standard_normal((3000, 32)).astype(np.float32)
