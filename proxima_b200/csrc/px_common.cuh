@@ -168,8 +168,53 @@ struct BlockTopK {
     }
   }
 
+  // k <= 32: warp w keeps stream w's k best in ascending order, with k rounds
+  // of a warp-wide minimum over the entries at or above `lo`, where lo is one
+  // past the last word taken. A stream's words are distinct (each row is
+  // offered to a stream once), so the rounds take the k smallest in order.
+  // About k*cnt/32 shared loads per lane, against a full bitonic sort of BUF
+  // words per stream. Used for buffers of 1024 words and more; on smaller
+  // ones the block-wide sort is shorter than one warp's serial rounds.
+  __device__ void select_small(int k, int tid, int nthreads) {
+    const int lane = tid & 31;
+    for (int g = tid >> 5; g < G; g += nthreads >> 5) {
+      uint64_t* b = buf + g * BUF;
+      const int n = cnt[g];
+      uint64_t mine = PX_EMPTY;  // lane r ends holding the r-th smallest
+      uint64_t lo = 0;
+      for (int r = 0; r < k; ++r) {
+        uint64_t m = PX_EMPTY;
+        for (int e = lane; e < n; e += 32) {
+          const uint64_t v = b[e];
+          if (v >= lo && v < m) m = v;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const uint64_t x = __shfl_xor_sync(0xffffffffu, m, o);
+          m = x < m ? x : m;
+        }
+        if (lane == r) mine = m;
+        if (m == PX_EMPTY) break;  // warp-uniform: fewer than k entries
+        lo = m + 1;
+      }
+      const uint64_t kth = __shfl_sync(0xffffffffu, mine, k - 1);
+      __syncwarp();
+      if (lane < k) b[lane] = mine;
+      if (lane == 0) {
+        const int c = n < k ? n : k;
+        cnt[g] = c;
+        thr[g] = (c == k) ? kth : PX_EMPTY;
+      }
+    }
+    __syncthreads();
+  }
+
   // Sorts every stream's buffer and keeps its k best. All threads.
   __device__ void compact_all(int k, int tid, int nthreads) {
+    if (BUF >= 1024 && k <= 32) {
+      select_small(k, tid, nthreads);
+      return;
+    }
     for (int i = tid; i < G * BUF; i += nthreads) {
       int g = i / BUF, e = i - g * BUF;
       if (e >= cnt[g]) buf[i] = PX_EMPTY;
