@@ -134,6 +134,20 @@ pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
     uint64_t thr4[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) thr4[j] = PX_EMPTY;
+    // The next iteration's filter bytes and codes, fetched one iteration
+    // ahead: every warp starts an iteration at the same barrier, so codes
+    // loaded there would leave the SM idle for a global-memory round trip.
+    uint4 nv[kRows];
+    bool nok[kRows];
+    auto fetch = [&](int64_t at) {
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        const int64_t row = at + r * (kPqThreads / 2) + qslot;
+        nok[r] = row < row_end && (mask == nullptr || mask[row] != 0);
+        nv[r] = nok[r] ? __ldg(reinterpret_cast<const uint4*>(codes + row * M)) : make_uint4(0, 0, 0, 0);
+      }
+    };
+    if (row_begin < row_end) fetch(row_begin);
     for (int64_t it = row_begin; it < row_end; it += kPqRowsPerIter) {
       bool ok[kRows];
       int64_t rr[kRows];
@@ -143,13 +157,13 @@ pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
 #pragma unroll
       for (int r = 0; r < kRows; ++r) {
         rr[r] = it + r * (kPqThreads / 2) + qslot;
-        ok[r] = rr[r] < row_end && (mask == nullptr || mask[rr[r]] != 0);
-        const uint4 v = ok[r] ? __ldg(reinterpret_cast<const uint4*>(codes + rr[r] * M)) : make_uint4(0, 0, 0, 0);
-        cw[1 + r * 4] = v.x;
-        cw[2 + r * 4] = v.y;
-        cw[3 + r * 4] = v.z;
-        cw[4 + r * 4] = v.w;
+        ok[r] = nok[r];
+        cw[1 + r * 4] = nv[r].x;
+        cw[2 + r * 4] = nv[r].y;
+        cw[3 + r * 4] = nv[r].z;
+        cw[4 + r * 4] = nv[r].w;
       }
+      if (it + kPqRowsPerIter < row_end) fetch(it + kPqRowsPerIter);
       // The code stream delayed by p bytes: byte i of sw is code byte i - p.
       uint32_t sw[kWords + 1];
 #pragma unroll
