@@ -350,7 +350,8 @@ def run_pq(args, cfg, rank, world, local_rank):
         "config": {"workload": WORKLOAD_TEXT[args.config], "n_codes": n, "dim": dim, "m": m, "nq": nq, "k": k,
                    "build_s": round(build_s, 2), "timing": "host-to-host PqIndex.search_batch"},
         "roofline": {"bound": "hbm", "achieved": byts / kern_s / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": byts / kern_s / 1e9 / pk["hbm_gbs"], "traffic": None, "kernel": "pq_scan_kernel",
+                     "frac": byts / kern_s / 1e9 / pk["hbm_gbs"], "traffic": ncu_traffic(args.config, "pq_scan_kernel"),
+                     "kernel": "pq_scan_kernel",
                      "kernel_ms": 1e3 * kern_s, "algorithmic_bytes_per_launch": byts,
                      "smem_gathers": {"achieved_per_ns": gathers / kern_s / 1e9, "peak_per_ns": smem_peak,
                                       "frac": gathers / kern_s / 1e9 / smem_peak,
