@@ -461,7 +461,11 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 #pragma unroll
       for (int j = 0; j < CAP; ++j) L[j] = PX_EMPTY;
       uint64_t thr = PX_EMPTY;
-      float thr_key = __int_as_float(0x7f800000);  // +inf: accept everything at first
+      const int64_t qidx = static_cast<int64_t>(qp * QT + wg) * BM + row_in_tile;
+      // +inf: accept everything at first. A padding query row (past nq) has
+      // all-zero products, hence equal keys that would all pass and take
+      // the rare insertion path on every step: -inf lets nothing in.
+      float thr_key = __int_as_float(qidx < p.nq ? 0x7f800000 : 0xff800000);
       int maxpos = 0;
       for (int t = t0; t < t1; ++t) {
         // Warp-uniform decision: the tcgen05.ld below is .sync.aligned.
@@ -487,7 +491,6 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       }
       if (!ok) break;
       list_sort<CAP>(L);
-      const int64_t qidx = static_cast<int64_t>(qp * QT + wg) * BM + row_in_tile;
       if (qidx < p.nq) {
         uint64_t* out = p.partial + (qidx * p.S + split) * CAP;
 #pragma unroll
@@ -715,7 +718,10 @@ gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
 #pragma unroll
       for (int j = 0; j < CAP; ++j) L[j] = PX_EMPTY;
       uint64_t thr = PX_EMPTY;
-      float thr_key = __int_as_float(0x7f800000);  // +inf: accept everything at first
+      const int64_t qidx = static_cast<int64_t>(qg) * (2 * PM) + static_cast<int64_t>(rank) * PM + row_in_tile;
+      // +inf: accept everything at first; -inf for a padding query row (see
+      // gemm_topk_kernel).
+      float thr_key = __int_as_float(qidx < p.nq ? 0x7f800000 : 0xff800000);
       int maxpos = 0;
       for (int t = t0; t < t1; ++t) {
         const bool got = __all_sync(0xffffffffu, tc::mbar_wait(tfull_bar(acc), acc_phase, s_abort, 256));
@@ -746,7 +752,6 @@ gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       }
       if (!ok) break;
       list_sort<CAP>(L);
-      const int64_t qidx = static_cast<int64_t>(qg) * (2 * PM) + static_cast<int64_t>(rank) * PM + row_in_tile;
       if (qidx < p.nq) {
         uint64_t* out = p.partial + ((qidx * p.S + split) * 2 + half) * CAP;
 #pragma unroll
