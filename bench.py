@@ -51,6 +51,8 @@ CONFIGS = {
     "c2q64": ("l2", 1_000_000, 128, 64, 10, "sift"),
     "c2q1": ("l2", 1_000_000, 128, 1, 10, "sift"),
     "c5": ("l2", 100_000_000, 96, 10_000, 10, "mixture"),
+    # config 5's distribution on a tenth of the rows (quick comparisons, ncu)
+    "c5s": ("l2", 10_000_000, 96, 10_000, 10, "mixture"),
     # profiling case for ncu: config 4's distribution and rows per split on 1/38 of the rows
     "prof": ("ip", 262_144, 768, 18_944, 10, "unit"),
     # PQ ADC scan (config 3): m=16 x 256 centroids trained on a 100k sample
@@ -64,6 +66,8 @@ WORKLOAD_TEXT = {
     "c2q64": "exact L2 kNN, base 1,000,000x128 SIFT-like, 64 queries, k=10 (config 2)",
     "c2q1": "exact L2 kNN, base 1,000,000x128 SIFT-like, 1 query, k=10 (config 2)",
     "c5": "exact L2 kNN, base 100,000,000x96 Gaussian mixture, one 10,000-query batch, k=10 (config 5)",
+    "c5s": ("config 5's distribution on a tenth of the rows: exact L2 kNN, base 10,000,000x96 Gaussian "
+            "mixture, 10,000 queries, k=10"),
     "prof": ("profiling case: exact IP kNN, base 262,144x768 unit-norm N(0,1), 18,944 queries, k=10 "
              "(2.8 GB on the device; 131k rows per split, as config 4 has 270k)"),
     "c3": "PQ ADC scan, L2, m=16 x 256 centroids (k-means on a 100,000-row sample), 1,000,000 codes, "

@@ -14,6 +14,17 @@
 // first candidate pass for small k; a flag records whether any value is not
 // exactly representable in bf16. `norms` holds the squared L2 norm of each
 // row for the approximate key ||x||^2 - 2 q.x.
+//
+// Folded L2 norms: where a row's bf16 padding has room (d + 3 <= ldb), the
+// bf16 copy of a shard row also carries its fp32 ||x||^2 in columns d, d+1,
+// d+2, split into three bf16 values whose sum is exact. Round-to-nearest
+// splitting leaves a remainder of at most 16 significant bits after the
+// first piece and at most 8 after the second, so the third is exact (for
+// norms above 2^-100, below which bf16 subnormals could drop bits). A query
+// converted for a folded L2 pass holds 2q (exact doubling) and -1 in those
+// columns, so its bf16 product with a row is 2 q.x - ||x||^2, the negated L2
+// key, and the inner-product epilogue serves the L2 pass. Any other query
+// holds zeros there, which leaves its products unchanged.
 #include <cuda_bf16.h>
 
 #include "px_common.cuh"
@@ -30,11 +41,12 @@ __device__ __forceinline__ float tf32_rn(float x) {
 }
 
 // One warp per row.
+// fold_query: convert query rows for a folded L2 pass (see above).
 __global__ void prepare_rows_kernel(const float* __restrict__ src, int64_t n, int d, int ld, int ldb,
                                     float* __restrict__ dst, float* __restrict__ hl,
                                     __nv_bfloat16* __restrict__ xb, float* __restrict__ norms,
                                     int* __restrict__ lo_nonzero, int* __restrict__ bf_inexact,
-                                    int* __restrict__ max_norm_sq) {
+                                    int* __restrict__ max_norm_sq, bool fold_query) {
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= n) return;
@@ -54,9 +66,10 @@ __global__ void prepare_rows_kernel(const float* __restrict__ src, int64_t n, in
       }
     }
     if (xb && e < ldb) {
-      const __nv_bfloat16 b = __float2bfloat16_rn(x);
+      const float xv = !fold_query ? x : (e < d ? __fmul_rn(2.0f, x) : (e < d + 3 ? -1.0f : 0.0f));
+      const __nv_bfloat16 b = __float2bfloat16_rn(xv);
       xb[row * ldb + e] = b;
-      bz |= (__bfloat162float(b) != x);
+      bz |= (__bfloat162float(b) != xv);
     }
   }
   __syncwarp();
@@ -78,6 +91,14 @@ __global__ void prepare_rows_kernel(const float* __restrict__ src, int64_t n, in
     for (int i = chunks * 8; i < d; ++i) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
     if (norms) norms[row] = s;
     if (max_norm_sq) atomicMax(max_norm_sq, __float_as_int(s));  // s >= 0: int order = float order
+    if (xb && d + 3 <= ldb) {  // shard row: the folded norm (the warp's zero padding is ordered before)
+      const __nv_bfloat16 h = __float2bfloat16_rn(s);
+      const float r1 = __fsub_rn(s, __bfloat162float(h));
+      const __nv_bfloat16 m = __float2bfloat16_rn(r1);
+      xb[row * ldb + d] = h;
+      xb[row * ldb + d + 1] = m;
+      xb[row * ldb + d + 2] = __float2bfloat16_rn(__fsub_rn(r1, __bfloat162float(m)));
+    }
   }
 }
 
@@ -108,20 +129,21 @@ cudaError_t launch_pack_mask(const uint8_t* mask, int64_t n, uint32_t* bits, cud
 
 cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, int ldb, float* dst, float* hl,
                                 void* xb, float* norms, int* lo_nonzero, int* bf_inexact, int* max_norm_sq,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, bool fold_query) {
   if (n == 0) return cudaSuccess;
   const int threads = 256;
   const int64_t blocks = (n * 32 + threads - 1) / threads;
   prepare_rows_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
       src, n, d, ld, ldb, dst, hl, static_cast<__nv_bfloat16*>(xb), norms, lo_nonzero, bf_inexact,
-      max_norm_sq);
+      max_norm_sq, fold_query);
   return cudaGetLastError();
 }
 
 cudaError_t launch_split_queries(const float* q, int64_t nq, int d, int ld, int ldb, int64_t rows_alloc,
-                                 float* hl, void* qb, int* lo_nonzero, int* bf_inexact, cudaStream_t stream) {
+                                 float* hl, void* qb, int* lo_nonzero, int* bf_inexact, cudaStream_t stream,
+                                 bool fold_l2) {
   cudaError_t e = launch_prepare_rows(q, nq, d, ld, ldb, nullptr, hl, qb, nullptr, lo_nonzero, bf_inexact,
-                                      nullptr, stream);
+                                      nullptr, stream, fold_l2);
   if (e != cudaSuccess) return e;
   if (rows_alloc > nq) {
     const int threads = 256;

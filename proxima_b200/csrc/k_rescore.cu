@@ -18,6 +18,12 @@
 // alone, 4 * 2^-22 * S for the three-pass tf32 sum), an allowance of
 // 2 * 2^-22 * S per tensor-core accumulation step (one per 8 values of K and
 // pass), and the rounding of the reference arithmetic and of the norms.
+// An L2 pass with folded norms accumulates 2 q.x - ||x||^2 (the norm as three
+// exact bf16 values in the rows' padding): the same terms doubled, so the
+// same bound on the key, plus the per-step allowance on the norm's share of
+// the partial sums, 2 * 2^-22 * max ||x||^2 per step, over three more K
+// values. Magnitudes near the exponent range (where the bf16 pieces or the
+// partial sums could overflow) are never certified.
 #include "px_common.cuh"
 #include "px_kernels.h"
 
@@ -140,7 +146,8 @@ rescore_kernel(const RescoreArgs a) {
         rep = 4.0 * 0x1p-22;
       }
     }
-    const double steps = static_cast<double>(npass) * ((a.d + 7) / 8) + 2.0;
+    const int dk = a.norm_folded ? a.d + 3 : a.d;  // K values with nonzero products
+    const double steps = static_cast<double>(npass) * ((dk + 7) / 8) + 2.0;
     const double S = qn * xn;
     const double e_dot = S * (rep + 2.0 * steps * 0x1p-22);
     const double ref = (a.d / 8 + 10) * 0x1p-23;
@@ -149,14 +156,14 @@ rescore_kernel(const RescoreArgs a) {
     double bound;
     if (L2) {
       const double qn2 = qn * qn;
-      const double eps = 2.0 * e_dot + xn * xn * ref + (qn + xn) * (qn + xn) * ref +
-                         (fabs(A) + qn2) * 0x1p-22;
+      double eps = 2.0 * e_dot + xn * xn * ref + (qn + xn) * (qn + xn) * ref + (fabs(A) + qn2) * 0x1p-22;
+      if (a.norm_folded) eps += 2.0 * steps * 0x1p-22 * xn * xn + 0x1p-120;
       bound = A + qn2 - eps;
     } else {
       const double eps = e_dot + S * ref + fabs(A) * 0x1p-22;
       bound = A - eps;
     }
-    ok = Ek < bound ? 1 : 0;
+    ok = (Ek < bound && S < 0x1p100 && xn * xn < 0x1p100) ? 1 : 0;
   }
   for (int j = lane; j < a.k; j += 32) a.out[q * a.k + j] = s_sorted[j];
   if (lane == 0) {

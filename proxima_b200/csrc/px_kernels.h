@@ -94,13 +94,17 @@ cudaError_t launch_nearest_centroid(const float* vectors, int64_t n, int m, int 
 // is raised when any lo element is nonzero, bf_inexact when any value
 // differs from its bf16 rounding; max_norm_sq (float bits) is raised to the
 // largest squared norm.
+// Shard rows (norms non-null) also carry their squared norm, split exactly
+// into three bf16 values, in bf16 columns d..d+2 when d + 3 <= ldb.
 cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, int ldb, float* dst, float* hl,
                                 void* xb, float* norms, int* lo_nonzero, int* bf_inexact, int* max_norm_sq,
-                                cudaStream_t stream);
+                                cudaStream_t stream, bool fold_query = false);
 // Split plane and bf16 plane of nq query rows (either may be null),
-// zero-filled up to rows_alloc rows.
+// zero-filled up to rows_alloc rows. fold_l2: the bf16 rows hold 2q and -1 in
+// columns d..d+2, so their product with a shard row is -(||x||^2 - 2 q.x).
 cudaError_t launch_split_queries(const float* q, int64_t nq, int d, int ld, int ldb, int64_t rows_alloc,
-                                 float* hl, void* qb, int* lo_nonzero, int* bf_inexact, cudaStream_t stream);
+                                 float* hl, void* qb, int* lo_nonzero, int* bf_inexact, cudaStream_t stream,
+                                 bool fold_l2 = false);
 
 // What a tensor-core candidate pass multiplies.
 enum PassKind : int {
@@ -169,6 +173,7 @@ struct RescoreArgs {
   int pass_kind;           // PassKind of the candidate pass
   int x_bf_inexact;        // shard values not all exact in bf16
   const int* q_bf_flag;    // device word: query values not all exact in bf16
+  int norm_folded;         // L2 keys came from bf16 rows carrying ||x||^2 (2 q.x - ||x||^2)
   uint64_t* out;           // [nq][k] exact candidates
   int* status;             // [nq] 0 = certified
   int* n_fail;             // count of uncertified queries

@@ -229,10 +229,14 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
                              const TensorWs& w, bool profile_main, cudaStream_t stream, int* n_fail,
                              bool* inexact) {
   const bool l2 = metric == PX_METRIC_L2;
+  // An L2 bf16 pass over rows that carry their norms in the padding runs as
+  // an inner product of 2q with them: no per-element norm term in the
+  // epilogue.
+  const bool folded = l2 && kind == kPassBf16 && h->dim + 3 <= h->ldb;
   cudaError_t e = cudaMemsetAsync(w.counters, 0, sizeof(int) * 4, stream);
   if (e == cudaSuccess)
     e = launch_split_queries(d_q, nq, h->dim, h->ld, h->ldb, plan.q_rows, w.q_hl, w.qb, w.counters + 1,
-                             w.counters + 3, stream);
+                             w.counters + 3, stream, folded);
   if (e != cudaSuccess) return cuda_status(e, "query split");
   GemmTopkArgs g;
   g.nq = static_cast<int>(nq);
@@ -245,7 +249,7 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
   g.tiles_per_split = plan.tiles_per_split;
   g.nb = plan.nb;
   g.n_items = plan.n_items;
-  g.l2 = l2;
+  g.l2 = l2 && !folded;
   g.norms = sh.norms;
   g.x_lo_nonzero = sh.lo_nonzero ? 1 : 0;
   g.q_lo_flag = w.counters + 1;
@@ -280,6 +284,7 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
   r.pass_kind = kind;
   r.x_bf_inexact = sh.bf_inexact ? 1 : 0;
   r.q_bf_flag = w.counters + 3;
+  r.norm_folded = folded ? 1 : 0;
   r.out = w.final_cands;
   r.status = w.status;
   r.n_fail = w.counters;

@@ -293,6 +293,25 @@ def test_tensor_path_parity(pxm, metric, n, dim, nq, k, path):
     assert prof["fallback_queries"] <= max(4, nq // 10), prof
 
 
+@pytest.mark.parametrize("dim", [96, 100, 29])
+def test_tensor_path_l2_folded_norms(pxm, dim):
+    # L2 with room in the bf16 padding (dim + 3 <= dim rounded up to 64):
+    # the rows carry ||x||^2 there and the bf16 pass runs as an inner
+    # product of 2q with them. Config 5's distribution certifies nearly
+    # every query; rows far from the origin (norms ~1e8 against distances
+    # ~1e2) make the folded sums large, and whatever the bound cannot
+    # certify must come out exact through the fallback.
+    data, queries = _data.gaussian_mixture(30000, 96, d=dim, centres=300, seed=dim)
+    ids, d, prof = _run_path(pxm, data, O.L2, queries, 10, "tensor")
+    assert prof["first_pass"] == "bf16"
+    _parity.check_flat(data, O.L2, queries, ids, d, 10)
+    assert prof["fallback_queries"] + prof["refined_queries"] <= max(4, len(queries) // 10), prof
+    far = (data + np.float32(1000.0)).astype(np.float32)
+    qfar = (queries + np.float32(1000.0)).astype(np.float32)
+    ids, d, prof = _run_path(pxm, far, O.L2, qfar, 10, "tensor")
+    _parity.check_flat(far, O.L2, qfar, ids, d, 10)
+
+
 def test_tensor_path_integer_data_single_pass(pxm):
     # Config 2's integer data: the tf32 lo planes are zero, one MMA pass is exact.
     data, queries = _data.sift_like(40000, 64, seed=11, centres=100)
