@@ -356,7 +356,13 @@ PX_API px_status px_flat_create(int32_t dim, int32_t metric, const int32_t* devi
   px_flat* h = new px_flat();
   h->dim = dim;
   h->ld = (dim + 31) & ~31;
+  // bf16 rows: dim rounded up to 64, so one 128-byte TMA row is one K slice.
+  // An L2 index of dim <= 256 also keeps room after the dim columns for each
+  // row's folded norm (three bf16 values): at small dim the bf16 pass is
+  // bound by its epilogue, and folding removes the epilogue's per-element
+  // norm term for at most one more K slice.
   h->ldb = (dim + 63) & ~63;
+  if (metric == PX_METRIC_L2 && dim <= 256 && dim + 3 > h->ldb) h->ldb += 64;
   h->metric = metric;
   h->shards.resize(devs.size());
   for (size_t i = 0; i < devs.size(); ++i) {

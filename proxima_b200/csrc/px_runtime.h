@@ -142,7 +142,7 @@ struct FlatSearchGraph {
 struct px_flat {
   int dim = 0;
   int ld = 0;   // fp32 / split-plane row stride: dim rounded up to 32
-  int ldb = 0;  // bf16 plane row stride: dim rounded up to 64
+  int ldb = 0;  // bf16 plane row stride: dim rounded up to 64 (plus 64 for a small-dim L2 index's folded norms)
   int metric = 0;
   int64_t total = 0;
   int64_t id_offset = 0;

@@ -293,10 +293,11 @@ def test_tensor_path_parity(pxm, metric, n, dim, nq, k, path):
     assert prof["fallback_queries"] <= max(4, nq // 10), prof
 
 
-@pytest.mark.parametrize("dim", [96, 100, 29])
+@pytest.mark.parametrize("dim", [96, 100, 29, 128, 62])
 def test_tensor_path_l2_folded_norms(pxm, dim):
-    # L2 with room in the bf16 padding (dim + 3 <= dim rounded up to 64):
-    # the rows carry ||x||^2 there and the bf16 pass runs as an inner
+    # L2 at dim <= 256: the bf16 rows carry ||x||^2 after the dim columns
+    # (in the padding, or in one more 64-column slice when the padding is
+    # too short, as for 128 and 62) and the bf16 pass runs as an inner
     # product of 2q with them. Config 5's distribution certifies nearly
     # every query; rows far from the origin (norms ~1e8 against distances
     # ~1e2) make the folded sums large, and whatever the bound cannot
