@@ -19,6 +19,10 @@ namespace {
 
 constexpr int kPqThreads = 512;       // 16 warps: enough to hide the LUT-gather latency
 constexpr int kPqRowsPerIter = 512;   // kSlots (threads / G) x G rows per thread
+// Candidate buffer of the m = 16, 8-query scan for k <= 32: 1,024 rows per
+// iteration (the most one iteration can add per query) plus 32. Its
+// compactions are warp selections, which need no power-of-two size.
+constexpr int kPqWideBuf = 1056;
 
 // 32-bit shared-memory load (the LUT gathers are the kernel's hot loop).
 __device__ __forceinline__ float lds_f32(uint32_t addr) {
@@ -116,7 +120,8 @@ pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
     // i, which is bank slice (i - p) % 4 -- four distinct slices, one
     // wavefront. Each thread streams its kRows rows' codes back to back; every
     // row still adds its subs in order 0..15 from 0.0, so keys are bit-exact.
-    constexpr int kRows = kPqRowsPerIter / (kPqThreads / 2);
+    constexpr int kIterRows = BUF == kPqWideBuf ? 1024 : kPqRowsPerIter;
+    constexpr int kRows = kIterRows / (kPqThreads / 2);
     constexpr int kWords = M * kRows / 4;  // code words of a thread's rows
     constexpr int kSkew = 3;
     constexpr int kSteps = M * kRows + kSkew;
@@ -148,7 +153,7 @@ pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
       }
     };
     if (row_begin < row_end) fetch(row_begin);
-    for (int64_t it = row_begin; it < row_end; it += kPqRowsPerIter) {
+    for (int64_t it = row_begin; it < row_end; it += kIterRows) {
       bool ok[kRows];
       int64_t rr[kRows];
       uint32_t cw[kWords + 2];  // cw[1 + w] = code word w; zero on both sides
@@ -163,7 +168,7 @@ pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
         cw[3 + r * 4] = nv[r].z;
         cw[4 + r * 4] = nv[r].w;
       }
-      if (it + kPqRowsPerIter < row_end) fetch(it + kPqRowsPerIter);
+      if (it + kIterRows < row_end) fetch(it + kIterRows);
       // The code stream delayed by p bytes: byte i of sw is code byte i - p.
       uint32_t sw[kWords + 1];
 #pragma unroll
@@ -201,7 +206,7 @@ pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
           if (ok[r] && quad * 4 + j < gcount)
             topk.offer(quad * 4 + j, pack_cand(fin[r][j], static_cast<uint32_t>(rr[r])), thr4[j]);
       __syncthreads();
-      topk.maybe_compact(k, kPqRowsPerIter, tid, kPqThreads);
+      topk.maybe_compact(k, kIterRows, tid, kPqThreads);
 #pragma unroll
       for (int j = 0; j < 4; ++j) thr4[j] = s_thr[quad * 4 + j];
     }
@@ -322,7 +327,8 @@ cudaError_t launch_pq_buf(const PqScanArgs& a, cudaStream_t stream) {
   }
 }
 
-int pq_buf_for(int k) {
+int pq_buf_for(int group, int m, int ksub, int k) {
+  if (group == 8 && m == 16 && ksub == 256 && k <= 32) return kPqWideBuf;
   if (k + kPqRowsPerIter <= 1024) return 1024;
   return 2048;
 }
@@ -355,8 +361,12 @@ __global__ void nearest_centroid_kernel(const float* __restrict__ vectors, int64
 
 int pq_max_k() { return 2048 - kPqRowsPerIter; }
 
+int pq_rows_per_iter(int group, int m, int ksub, int k) {
+  return pq_buf_for(group, m, ksub, k) == kPqWideBuf ? 1024 : kPqRowsPerIter;
+}
+
 size_t pq_smem_for(int group, int m, int ksub, int k) {
-  const int buf = pq_buf_for(k);
+  const int buf = pq_buf_for(group, m, ksub, k);
   return sizeof(uint64_t) * (group * buf + ((group + 1) & ~1)) + sizeof(int) * ((group + 3) & ~3) +
          sizeof(float) * static_cast<size_t>(group) * m * ksub;
 }
@@ -376,7 +386,9 @@ cudaError_t launch_pq_lut(const float* books, int m, int ksub, int dsub, bool l2
 }
 
 cudaError_t launch_pq_scan(const PqScanArgs& a, cudaStream_t stream) {
-  if (pq_buf_for(a.k) == 1024) return launch_pq_buf<1024>(a, stream);
+  const int buf = pq_buf_for(a.group, a.m, a.ksub, a.k);
+  if (buf == kPqWideBuf) return launch_pq_gm<8, kPqWideBuf, 16>(a, stream);
+  if (buf == 1024) return launch_pq_buf<1024>(a, stream);
   return launch_pq_buf<2048>(a, stream);
 }
 

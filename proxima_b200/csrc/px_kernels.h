@@ -78,6 +78,8 @@ struct PqScanArgs {
 cudaError_t launch_pq_scan(const PqScanArgs& a, cudaStream_t stream);
 int pq_group_for(int m, int ksub, int64_t nq, int k);
 size_t pq_smem_for(int group, int m, int ksub, int k);
+// Rows one scan iteration covers; a CTA's row range is a multiple of it.
+int pq_rows_per_iter(int group, int m, int ksub, int k);
 int pq_max_k();
 
 // Nearest centroid per (vector, subspace) with the reference's strict '<'

@@ -178,8 +178,9 @@ static px_status pq_shard_search(const px_pq* h, PqShard& sh, const float* d_q, 
     }
     if (fill >= 0.97) break;
   }
+  const int64_t rpi = pq_rows_per_iter(group, h->m, h->ksub, k);
   int64_t rows = (n + ncta - 1) / ncta;
-  rows = (rows + 511) / 512 * 512;
+  rows = (rows + rpi - 1) / rpi * rpi;
   ncta = (n + rows - 1) / rows;
 
   px::Carver c;
