@@ -67,6 +67,9 @@ __global__ void pq_lut_kernel(const float* __restrict__ books, int m, int ksub, 
 // so a warp's gathers touch at most 32/G distinct 32-word rows.
 // M > 0: m == M (a multiple of 16) and ksub == 256, so table offsets and
 // code byte positions are compile-time constants; M == 0: any m and ksub.
+// M == 16 with G == 8 (the common case) takes the skewed schedule below, over
+// a [sub/8][code][sub%8][query] table; with BUF == kPqWideBuf (k <= 32) it
+// covers 1,024 rows per iteration instead of 512.
 template <int G, int BUF, int M>
 __global__ void __launch_bounds__(kPqThreads)
 pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
