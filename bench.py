@@ -567,7 +567,8 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c4k10")
     ap.add_argument("--seed", type=int, default=2024)
-    ap.add_argument("--cpu-sample", type=int, default=32, help="queries timed on the CPU baseline")
+    ap.add_argument("--cpu-sample", type=int, default=112,
+                    help="queries timed on the CPU baseline; also the parity sample")
     ap.add_argument("--ref-sample", type=int, default=16, help="queries per step of --impl reference")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--path", choices=["auto", "exact", "tensor", "tensor_3xtf32"], default="auto",
