@@ -253,6 +253,8 @@ def run_reference(args, cfg, rank, world):
     device = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
     base = host_copy(kind, n, dim, args.seed, device)
     queries = gen_queries(kind, nq, dim, args.seed, device).cpu().numpy()
+    if metric.startswith("pq"):
+        return run_reference_pq(args, cfg, world, base, queries)
     sample = args.ref_sample
     for _ in range(args.warmup):
         cpu_sample_qps(base, metric, queries[:max(1, sample // 4)], k, max(1, sample // 4))
@@ -273,6 +275,38 @@ def run_reference(args, cfg, rank, world):
                          "sample": f"{sample} queries per step against the full {n}x{dim} base; "
                                    "C++ restatement of FlatIndex::search_batch (flat.rs:150-191), "
                                    "all host threads (the Rust crate cannot be built here)"},
+        "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_reference_pq(args, cfg, world, base, queries):
+    """--impl reference for config 3: codebooks and codes from the oracle's
+    restatement of ProductQuantizer::train / encode_into with the parameters
+    the GPU arm uses (so both scan the same codes), then the oracle's
+    PqIndex::search_batch over all queries each step."""
+    import oracle as O
+    metric, n, dim, nq, k, kind = cfg
+    books = O.pq_train(base, 16, nbits=8, train_iters=25, train_sample=100_000, seed=args.seed)
+    codes = O.pq_encode(books, base)
+    for _ in range(args.warmup):
+        O.pq_search_batch(books, O.L2, codes, queries[:max(1, nq // 8)], k, num_threads=host_cores())
+    times = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        O.pq_search_batch(books, O.L2, codes, queries, k, num_threads=host_cores())
+        times.append(time.perf_counter() - t)
+    value = nq * args.steps / sum(times)
+    line = {
+        "metric": f"PQ ADC QPS (k={k})", "value": value, "unit": "queries/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (u8 codes)",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD_TEXT[args.config], "n_codes": n, "dim": dim, "m": 16, "nq": nq, "k": k},
+        "cpu_baseline": {"value": value, "unit": "queries/s", "cores": cpu_threads(), "kind": "port",
+                         "sample": f"all {nq} queries per step against all {n} codes; C++ restatement of "
+                                   "PqIndex::search_batch (pq.rs:349-396), all host threads"},
         "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
