@@ -179,6 +179,20 @@ PX_API px_status px_flat_search_noalloc(const float* d_base, int64_t n, int32_t 
                                         const float* d_queries, int64_t nq, int32_t k,
                                         int64_t* d_out_ids, float* d_out_dists, void* stream);
 
+/* Instrumentation, no counterpart in the reference: runs only the first
+ * tensor-core candidate pass of a search (single-device handle, 1 <= k <=
+ * 224, any path mode but EXACT treated as TENSOR) for nq host queries and
+ * writes, per query, its merged candidates before exact rescoring: up to
+ * max_cands ids (padding -1) with their APPROXIMATE keys as the pass computed
+ * them (-q~.x~ for inner product; ||x||^2 - 2 q~.x~ for L2, without ||q||^2),
+ * sorted by that key. *out_cands = candidates written per query, *out_pass =
+ * the pass's operands (0 three-pass tf32, 1 tf32, 2 bf16). Tests use it to
+ * measure the tensor cores' accumulation error against the bound the
+ * certificate assumes. */
+PX_API px_status px_flat_debug_candidates(const px_flat* h, const float* queries, int64_t nq, int32_t k,
+                                          int32_t max_cands, int64_t* out_ids, float* out_keys,
+                                          int32_t* out_cands, int32_t* out_pass);
+
 /* Cross-shard merge on one device: keys/ids [nshard][nq][k] in key space,
  * each list sorted; writes the k best per query (ties by smaller id) as
  * natural distances (natural != 0) or keys. */

@@ -75,6 +75,7 @@ SIGNATURES = {
     "px_flat_search_filtered": (_i32, [_vp, _f32p, _i64, _i32, _u8p, _i64p, _f32p]),
     "px_flat_search_device": (_i32, [_vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp]),
     "px_flat_search_noalloc": (_i32, [_vp, _i64, _i32, _i32, _vp, _i64, _i32, _vp, _vp, _vp]),
+    "px_flat_debug_candidates": (_i32, [_vp, _f32p, _i64, _i32, _i32, _i64p, _f32p, _i32p, _i32p]),
     "px_merge_shards_device": (_i32, [_i32, _vp, _vp, _i32, _i64, _i32, _i32, _i32, _vp, _vp, _vp]),
     "px_pq_train": (_i32, [_f32p, _i64, _i32, _i32, _i32, _i32, _i64, _u64, _i32, _f32p]),
     "px_pq_create": (_i32, [_i32, _i32, _i32, _i32, _f32p, _i32p, _i32, _c.POINTER(_vp)]),

@@ -2,7 +2,7 @@
 //
 // The fp32 rows are kept as given (the exact rescoring and the streaming scan
 // read them); beside them each row is split for the 3xTF32 contraction:
-//   hi = tf32_rn(x),  lo = tf32_rn(x - hi)      (x - hi is exact in fp32)
+//   hi = tf32_rna(x),  lo = tf32_rna(x - hi)      (x - hi is exact in fp32)
 // so that q.x ~= qhi.xhi + qhi.xlo + qlo.xhi with an error of a few 2^-22
 // relative per product. The split plane interleaves the two halves per
 // 16-element chunk -- [hi x16 | lo x16], 128 bytes -- so one 128-byte TMA row
@@ -34,42 +34,54 @@ namespace px {
 
 namespace {
 
-__device__ __forceinline__ float tf32_rn(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
+// An upper bound, as a float, on the square root of a sum of squares that
+// was accumulated in double (each square exact, at most a few dozen adds):
+// the relative margin dwarfs double rounding, and both conversions round up.
+__device__ __forceinline__ float sqrt_up(double sum_sq) {
+  return __double2float_ru(__dsqrt_ru(sum_sq * (1.0 + 0x1p-40)));
 }
 
 // One warp per row.
 // fold_query: convert query rows for a folded L2 pass (see above).
+// resid (shard rows): resid[0] / resid[1] are raised (float bits) to an upper
+// bound on ||x - bf16(x)|| / ||x - tf32_hi(x)|| over the row's d values, the
+// per-row representation errors the certificate of a bf16 / tf32 candidate
+// pass bounds the shard's contribution by.
 __global__ void prepare_rows_kernel(const float* __restrict__ src, int64_t n, int d, int ld, int ldb,
                                     float* __restrict__ dst, float* __restrict__ hl,
                                     __nv_bfloat16* __restrict__ xb, float* __restrict__ norms,
                                     int* __restrict__ lo_nonzero, int* __restrict__ bf_inexact,
-                                    int* __restrict__ max_norm_sq, bool fold_query) {
+                                    int* __restrict__ max_norm_sq, bool fold_query, int* __restrict__ resid) {
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= n) return;
   bool nz = false, bz = false;
+  // x - bf16(x) and x - tf32(x) are exact in fp32, and their squares exact in
+  // double.
+  double rb = 0.0, rt = 0.0;
   const int width = ldb > ld ? ldb : ld;
   for (int e = lane; e < width; e += 32) {
     float x = e < d ? src[row * d + e] : 0.f;
     if (e < ld) {
       if (dst) dst[row * ld + e] = x;
       if (hl) {
-        const float h = tf32_rn(x);
-        const float l = tf32_rn(__fsub_rn(x, h));
-        float* r = hl + row * 2 * ld + (e >> 4) * 32 + (e & 15);
-        r[0] = h;
-        r[16] = l;
+        const float h = tf32_rna(x);
+        const float r = __fsub_rn(x, h);
+        const float l = tf32_rna(r);
+        float* p = hl + row * 2 * ld + (e >> 4) * 32 + (e & 15);
+        p[0] = h;
+        p[16] = l;
         nz |= (l != 0.f);
+        rt += static_cast<double>(r) * r;
       }
     }
     if (xb && e < ldb) {
       const float xv = !fold_query ? x : (e < d ? __fmul_rn(2.0f, x) : (e < d + 3 ? -1.0f : 0.0f));
       const __nv_bfloat16 b = __float2bfloat16_rn(xv);
       xb[row * ldb + e] = b;
-      bz |= (__bfloat162float(b) != xv);
+      const float r = __fsub_rn(xv, __bfloat162float(b));
+      bz |= (r != 0.f);
+      rb += static_cast<double>(r) * r;
     }
   }
   __syncwarp();
@@ -77,6 +89,18 @@ __global__ void prepare_rows_kernel(const float* __restrict__ src, int64_t n, in
   const bool any_bz = __any_sync(0xffffffffu, bz);
   if (lo_nonzero && any_nz && lane == 0) atomicOr(lo_nonzero, 1);
   if (bf_inexact && any_bz && lane == 0) atomicOr(bf_inexact, 1);
+  if (resid) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      rb += __shfl_xor_sync(0xffffffffu, rb, off);
+      rt += __shfl_xor_sync(0xffffffffu, rt, off);
+    }
+    // Non-negative floats order like their bit patterns as ints.
+    if (lane == 0) {
+      atomicMax(resid, __float_as_int(sqrt_up(rb)));
+      atomicMax(resid + 1, __float_as_int(sqrt_up(rt)));
+    }
+  }
   if ((norms || max_norm_sq) && lane == 0) {
     // Squared norm in the reference's 8-lane order (l2_sqr(x, 0)).
     const float* x = (dst ? dst + row * ld : src + row * d);
@@ -129,13 +153,13 @@ cudaError_t launch_pack_mask(const uint8_t* mask, int64_t n, uint32_t* bits, cud
 
 cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, int ldb, float* dst, float* hl,
                                 void* xb, float* norms, int* lo_nonzero, int* bf_inexact, int* max_norm_sq,
-                                cudaStream_t stream, bool fold_query) {
+                                cudaStream_t stream, bool fold_query, int* resid) {
   if (n == 0) return cudaSuccess;
   const int threads = 256;
   const int64_t blocks = (n * 32 + threads - 1) / threads;
   prepare_rows_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
       src, n, d, ld, ldb, dst, hl, static_cast<__nv_bfloat16*>(xb), norms, lo_nonzero, bf_inexact,
-      max_norm_sq, fold_query);
+      max_norm_sq, fold_query, resid);
   return cudaGetLastError();
 }
 

@@ -11,19 +11,43 @@
 //   exact_k < A - eps (strict, so no outside row can even tie).
 // A query whose certificate fails is listed for the exact streaming scan.
 //
-// eps is a worst-case bound, in double precision, built from
-//   S = ||q|| * max_x ||x|| >= sum_i |q_i x_i|        (Cauchy-Schwarz)
-// the representation error of the pass's operands (zero when they are exact:
-// (2^-8 + 2^-18) * S for bf16 copies, (2^-10 + 2^-22) * S for tf32 hi values
-// alone, 4 * 2^-22 * S for the three-pass tf32 sum), an allowance of
-// 2 * 2^-22 * S per tensor-core accumulation step (one per 8 values of K and
-// pass), and the rounding of the reference arithmetic and of the norms.
-// An L2 pass with folded norms accumulates 2 q.x - ||x||^2 (the norm as three
-// exact bf16 values in the rows' padding): the same terms doubled, so the
-// same bound on the key, plus the per-step allowance on the norm's share of
-// the partial sums, 2 * 2^-22 * max ||x||^2 per step, over three more K
-// values. Magnitudes near the exponent range (where the bf16 pieces or the
-// partial sums could overflow) are never certified.
+// eps is a worst-case bound, evaluated in double precision, with three parts.
+//
+// 1. Representation. The pass multiplies rounded copies q~, x~ of the query
+//    and the rows. Exactly, q.x - q~.x~ = (q - q~).x + q~.(x - x~), so by
+//    Cauchy-Schwarz
+//        |q.x - q~.x~| <= ||q - q~|| * max||x|| + ||q~|| * max||x - x~||.
+//    The query terms are computed here from the query itself (with the same
+//    rounding the conversion kernel applies: bf16 round-to-nearest-even, or
+//    tf32 round-to-nearest-away); max||x - x~|| is an upper bound the shard
+//    build keeps (k_prep.cu). Both are zero for data exact in the pass's
+//    format (e.g. small integers). For the three-pass tf32 sum
+//    qh.xh + qh.xl + ql.xh the dropped terms are qh.rx + ql.(x - xh) + rq.x
+//    (rx, rq: the tf32 rounding of the lo parts), each at most
+//    2^-22 * sum|q_i x_i| (+ 2^-33), so 4 * 2^-22 * S bounds them, with
+//    S = ||q|| * max||x|| >= sum|q_i x_i|.
+// 2. Accumulation. The tensor core's products of bf16 or tf32 values are
+//    exact in fp32. The sums are modelled as any sequence of steps, each
+//    adding c >= 1 products to the fp32 accumulator with every operand
+//    aligned to the largest one and cut to 24 significant bits (at most one
+//    unit in the last place of the largest operand lost per operand), then
+//    the sum rounded or cut to 24 bits (another unit). Every operand and
+//    partial sum is at most M = sum of the magnitudes of all products, so a
+//    step loses at most (c + 2) * 2^-23 * M, i.e. at most 3 * 2^-23 * M per
+//    product whatever the hardware's grouping: the model assumes only that
+//    no operand keeps fewer than 24 bits relative to the largest operand of
+//    its step. M = S (x 1.01 for the rounded copies' own growth); a folded L2
+//    pass accumulates 2 q~.x~ - ||x||^2 (its norm as three exact bf16 values
+//    in the rows' padding), so M = 2.02 S + max||x||^2 there. Products that
+//    underflow fp32 add at most 2^-120 * (1 + ||q|| + max||x||) each.
+// 3. Reference and epilogue rounding: the reference key's own fp32 rounding
+//    (8-lane order, relative (d/8 + 10) * 2^-23 of the sum of the terms'
+//    magnitudes), the fp32 row norms, and the epilogue's rounding of the
+//    approximate key (|A| * 2^-22).
+// Magnitudes near the exponent range (where the bf16 pieces or the partial
+// sums could overflow) are never certified.
+#include <cuda_bf16.h>
+
 #include "px_common.cuh"
 #include "px_kernels.h"
 
@@ -48,14 +72,30 @@ rescore_kernel(const RescoreArgs a) {
   if (q >= a.nq) return;
 
   const float* qv = a.queries + q * a.d;
-  double qsq = 0.0;
+  // ||q||^2, and for a bf16 or tf32 pass ||q' - q'~||^2 and ||q'~||^2, where
+  // q' is what the query conversion rounds (2q for a folded L2 pass; the
+  // doubling is exact) and q'~ its rounding. Squares of fp32 values and of
+  // their exact rounding residuals are exact in double.
+  const bool folded = a.norm_folded != 0;
+  double qsq = 0.0, rq2 = 0.0, qt2 = 0.0;
   for (int i = lane; i < a.d; i += 32) {
     const float v = qv[i];
     s_q[i] = v;
     qsq += static_cast<double>(v) * v;
+    const float u = folded ? __fmul_rn(2.0f, v) : v;
+    float t = u;
+    if (a.pass_kind == kPassBf16) t = __bfloat162float(__float2bfloat16_rn(u));
+    else if (a.pass_kind == kPassTf32) t = tf32_rna(u);
+    const double r = static_cast<double>(__fsub_rn(u, t));
+    rq2 += r * r;
+    qt2 += static_cast<double>(t) * t;
   }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) qsq += __shfl_xor_sync(0xffffffffu, qsq, off);
+  for (int off = 16; off > 0; off >>= 1) {
+    qsq += __shfl_xor_sync(0xffffffffu, qsq, off);
+    rq2 += __shfl_xor_sync(0xffffffffu, rq2, off);
+    qt2 += __shfl_xor_sync(0xffffffffu, qt2, off);
+  }
   __syncwarp();
 
   // Exact keys, four candidates at a time: thread l of a group of eight runs
@@ -127,43 +167,41 @@ rescore_kernel(const RescoreArgs a) {
     // Fewer than k candidates, yet a full list may hide rows: not certified.
     ok = 0;
   } else if (last != PX_EMPTY) {
-    const double qn = sqrt(qsq);
-    const double xn = static_cast<double>(a.max_norm);
+    const double ref = (a.d / 8 + 10) * 0x1p-23;  // the reference's relative rounding
+    const double qn = sqrt(qsq) * (1.0 + 0x1p-40);
+    // Upper bound on every row's real norm: the shard keeps the largest fp32
+    // norm, itself rounded in the reference's order.
+    const double xn2 = static_cast<double>(a.max_norm_sq) * (1.0 + ref);
+    const double xn = sqrt(xn2) * (1.0 + 0x1p-40);
+    const double S = qn * xn;
     const bool q_lo = *a.q_lo_flag != 0;
     int npass = 1;
-    double rep = 0.0;  // representation error per product, relative to |q_i x_i|
-    if (a.pass_kind == kPassBf16) {
-      // Each bf16 value is within 2^-9 of its fp32 value: (1 + 2^-9)^2 - 1.
-      if (*a.q_bf_flag != 0 || a.x_bf_inexact) rep = 0x1p-8 + 0x1p-18;
+    double e_rep = 0.0;  // bound on |q'.x - (the pass's product of the rounded copies)|
+    if (a.pass_kind == kPassBf16 || a.pass_kind == kPassTf32) {
+      e_rep = (sqrt(rq2) * xn + sqrt(qt2) * static_cast<double>(a.x_resid)) * (1.0 + 0x1p-40);
     } else if (q_lo || a.x_lo_nonzero) {
-      if (a.pass_kind == kPassTf32) {
-        // hi x hi alone: each hi is within 2^-11 of its value.
-        rep = 0x1p-10 + 0x1p-22;
-      } else {
-        // Three-pass sum: the dropped lo x lo term and the tf32 rounding of
-        // each lo.
-        npass = 1 + (q_lo ? 1 : 0) + (a.x_lo_nonzero ? 1 : 0);
-        rep = 4.0 * 0x1p-22;
-      }
+      npass = 1 + (q_lo ? 1 : 0) + (a.x_lo_nonzero ? 1 : 0);
+      e_rep = 4.0 * 0x1p-22 * S;
     }
-    const int dk = a.norm_folded ? a.d + 3 : a.d;  // K values with nonzero products
-    const double steps = static_cast<double>(npass) * ((dk + 7) / 8) + 2.0;
-    const double S = qn * xn;
-    const double e_dot = S * (rep + 2.0 * steps * 0x1p-22);
-    const double ref = (a.d / 8 + 10) * 0x1p-23;
+    const int dk = folded ? a.d + 3 : a.d;  // K values with nonzero products
+    const double products = static_cast<double>(npass) * dk + 2.0;
+    const double M = folded ? 2.02 * S + xn2 : 1.01 * S;
+    const double e_acc = 3.0 * 0x1p-23 * products * M + products * (1.0 + qn + xn) * 0x1p-120;
     const double A = static_cast<double>(cand_key(last));
     const double Ek = static_cast<double>(cand_key(kth));
     double bound;
     if (L2) {
+      // Folded: the pass's key is -(2q~.x~ - ||x||^2) and e_rep already
+      // bounds the doubled product; otherwise ||x||^2 - 2 q~.x~.
       const double qn2 = qn * qn;
-      double eps = 2.0 * e_dot + xn * xn * ref + (qn + xn) * (qn + xn) * ref + (fabs(A) + qn2) * 0x1p-22;
-      if (a.norm_folded) eps += 2.0 * steps * 0x1p-22 * xn * xn + 0x1p-120;
+      const double e_key = folded ? e_rep + e_acc : 2.0 * (e_rep + e_acc);
+      const double eps = e_key + xn2 * ref + (qn + xn) * (qn + xn) * ref + (fabs(A) + qn2) * 0x1p-22;
       bound = A + qn2 - eps;
     } else {
-      const double eps = e_dot + S * ref + fabs(A) * 0x1p-22;
+      const double eps = e_rep + e_acc + S * ref + fabs(A) * 0x1p-22;
       bound = A - eps;
     }
-    ok = (Ek < bound && S < 0x1p100 && xn * xn < 0x1p100) ? 1 : 0;
+    ok = (Ek < bound && S < 0x1p100 && xn2 < 0x1p100) ? 1 : 0;
   }
   for (int j = lane; j < a.k; j += 32) a.out[q * a.k + j] = s_sorted[j];
   if (lane == 0) {

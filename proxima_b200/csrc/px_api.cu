@@ -304,7 +304,7 @@ px_status FlatShard::append_device(const float* d_src, int64_t count, int d, int
   if (s != PX_OK) return s;
   cudaError_t e = launch_prepare_rows(d_src, count, d, ld, ldb, x + n * ld, hl + n * 2 * ld,
                                       static_cast<uint16_t*>(xb) + n * ldb, norms + n, flag, flag + 1,
-                                      flag + 2, stream);
+                                      flag + 2, stream, false, flag + 3);
   if (e != cudaSuccess) return cuda_status(e, "prepare_rows launch");
   segs.local.push_back(n);
   segs.global.push_back(global_begin);
@@ -312,12 +312,14 @@ px_status FlatShard::append_device(const float* d_src, int64_t count, int d, int
   n += count;
   e = cudaStreamSynchronize(stream);
   if (e != cudaSuccess) return cuda_status(e, "add");
-  int h_flag[4] = {0, 0, 0, 0};
+  int h_flag[kShardFlags] = {};
   e = cudaMemcpy(h_flag, flag, sizeof(h_flag), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_status(e, "add flag readback");
   lo_nonzero = h_flag[0] != 0;
   bf_inexact = h_flag[1] != 0;
   std::memcpy(&max_norm_sq, &h_flag[2], sizeof(float));
+  std::memcpy(&bf_resid, &h_flag[3], sizeof(float));
+  std::memcpy(&tf_resid, &h_flag[4], sizeof(float));
   g_launches += 1;
   return PX_OK;
 }
@@ -370,8 +372,8 @@ PX_API px_status px_flat_create(int32_t dim, int32_t metric, const int32_t* devi
     sh.device = devs[i];
     DeviceGuard g(sh.device);
     cudaError_t e = cudaStreamCreateWithFlags(&sh.stream, cudaStreamNonBlocking);
-    if (e == cudaSuccess) e = cudaMalloc(&sh.flag, 4 * sizeof(int));
-    if (e == cudaSuccess) e = cudaMemset(sh.flag, 0, 4 * sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&sh.flag, kShardFlags * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(sh.flag, 0, kShardFlags * sizeof(int));
     if (e == cudaSuccess) e = cudaEventCreate(&sh.ev_start);
     if (e == cudaSuccess) e = cudaEventCreate(&sh.ev_stop);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sh.ev_done, cudaEventDisableTiming);
@@ -876,6 +878,60 @@ PX_API px_status px_flat_search_device(const px_flat* hc, const float* d_queries
   // would not be ordered with the caller's collectives and merges.
   return shard_search(h, sh, h->metric, d_queries, nq, k, nullptr, key_space == 0, d_out_ids,
                       d_out_dists, static_cast<cudaStream_t>(stream));
+}
+
+PX_API px_status px_flat_debug_candidates(const px_flat* hc, const float* queries, int64_t nq, int32_t k,
+                                          int32_t max_cands, int64_t* out_ids, float* out_keys,
+                                          int32_t* out_cands, int32_t* out_pass) {
+  px_status s = validate_search(hc, queries, nq, k, out_ids, out_keys);
+  if (s != PX_OK) return s;
+  if (hc->shards.size() != 1)
+    return set_error(PX_EUNSUPPORTED, "px_flat_debug_candidates needs a single-device handle");
+  if (max_cands < 1 || out_cands == nullptr || out_pass == nullptr)
+    return set_error(PX_EINVAL, "max_cands must be >= 1 and out_cands / out_pass non-null");
+  if (k < 1 || nq < 1) return set_error(PX_EINVAL, "k and the query count must be >= 1");
+  if (!all_finite(queries, nq * hc->dim))
+    return set_error(PX_EINVAL, "query must not contain NaN or infinite values");
+  px_flat* h = const_cast<px_flat*>(hc);
+  std::lock_guard<std::mutex> lk(h->mu);
+  FlatShard& sh = h->shards[0];
+  DeviceGuard dg(sh.device);
+  const size_t qbytes = sizeof(float) * static_cast<size_t>(nq) * h->dim;
+  cudaError_t e = sh.stage.reserve(qbytes);
+  if (e != cudaSuccess) return cuda_status(e, "query staging allocation");
+  e = cudaMemcpyAsync(sh.stage.ptr, queries, qbytes, cudaMemcpyHostToDevice, sh.stream);
+  if (e != cudaSuccess) return cuda_status(e, "query upload");
+  const uint64_t* d_merged = nullptr;
+  int cands = 0, pass = 0;
+  s = first_pass_candidates(h, sh, h->metric, static_cast<const float*>(sh.stage.ptr), nq, k, sh.stream,
+                            &d_merged, &cands, &pass);
+  if (s != PX_OK) return s;
+  std::vector<uint64_t> merged(static_cast<size_t>(nq) * cands);
+  e = cudaMemcpyAsync(merged.data(), d_merged, merged.size() * sizeof(uint64_t), cudaMemcpyDeviceToHost,
+                      sh.stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(sh.stream);
+  if (e != cudaSuccess) return cuda_status(e, "candidate readback");
+  const int m = std::min(cands, max_cands);
+  for (int64_t q = 0; q < nq; ++q) {
+    for (int j = 0; j < max_cands; ++j) {
+      const size_t o = static_cast<size_t>(q) * max_cands + j;
+      const uint64_t c = j < m ? merged[static_cast<size_t>(q) * cands + j] : PX_EMPTY;
+      if (c == PX_EMPTY) {
+        out_ids[o] = -1;
+        out_keys[o] = 3.40282347e+38f;
+        continue;
+      }
+      // Shard row -> global id through the segment table.
+      const int64_t row = cand_row(c);
+      size_t seg = 0;
+      while (seg + 1 < sh.segs.local.size() && sh.segs.local[seg + 1] <= row) ++seg;
+      out_ids[o] = sh.segs.global[seg] + (row - sh.segs.local[seg]) + h->id_offset;
+      out_keys[o] = cand_key(c);
+    }
+  }
+  *out_cands = m;
+  *out_pass = pass;
+  return PX_OK;
 }
 
 PX_API px_status px_merge_shards_device(int32_t device, const float* d_keys, const int64_t* d_ids,

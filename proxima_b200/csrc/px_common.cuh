@@ -51,6 +51,14 @@ __host__ __device__ __forceinline__ uint32_t cand_row(uint64_t c) {
   return static_cast<uint32_t>(c & 0xFFFFFFFFu);
 }
 
+// x rounded to tf32 (10 stored mantissa bits), to nearest with ties away from
+// zero: the hi part of the three-pass split.
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
 // Natural distance reported to callers (flat.rs:142, 146; pq.rs:335-345).
 __device__ __forceinline__ float natural_dist(float key, bool l2) {
   return l2 ? __fsqrt_rn(key) : -key;

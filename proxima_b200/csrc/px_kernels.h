@@ -98,9 +98,11 @@ cudaError_t launch_nearest_centroid(const float* vectors, int64_t n, int m, int 
 // largest squared norm.
 // Shard rows (norms non-null) also carry their squared norm, split exactly
 // into three bf16 values, in bf16 columns d..d+2 when d + 3 <= ldb.
+// resid (optional, two words of float bits): raised to upper bounds on the
+// largest ||x - bf16(x)|| and ||x - tf32_hi(x)|| of the rows.
 cudaError_t launch_prepare_rows(const float* src, int64_t n, int d, int ld, int ldb, float* dst, float* hl,
                                 void* xb, float* norms, int* lo_nonzero, int* bf_inexact, int* max_norm_sq,
-                                cudaStream_t stream, bool fold_query = false);
+                                cudaStream_t stream, bool fold_query = false, int* resid = nullptr);
 // Split plane and bf16 plane of nq query rows (either may be null),
 // zero-filled up to rows_alloc rows. fold_l2: the bf16 rows hold 2q and -1 in
 // columns d..d+2, so their product with a shard row is -(||x||^2 - 2 q.x).
@@ -169,12 +171,12 @@ struct RescoreArgs {
   int ld;
   int d;
   bool l2;
-  float max_norm;          // max ||x|| over the shard
+  float max_norm_sq;       // max over the shard of the rows' fp32 squared norms
+  float x_resid;           // upper bound on max ||x - x~|| over the shard, x~ the rows as
+                           // the pass multiplies them (bf16, or tf32 hi values)
   int x_lo_nonzero;
   const int* q_lo_flag;
   int pass_kind;           // PassKind of the candidate pass
-  int x_bf_inexact;        // shard values not all exact in bf16
-  const int* q_bf_flag;    // device word: query values not all exact in bf16
   int norm_folded;         // L2 keys came from bf16 rows carrying ||x||^2 (2 q.x - ||x||^2)
   uint64_t* out;           // [nq][k] exact candidates
   int* status;             // [nq] 0 = certified

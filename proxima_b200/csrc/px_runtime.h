@@ -15,6 +15,7 @@
 namespace px {
 
 extern thread_local std::string g_last_error;
+constexpr int kShardFlags = 8;  // words of FlatShard::flag
 px_status set_error(px_status s, const std::string& msg);
 px_status cuda_status(cudaError_t e, const char* what);
 bool all_finite(const float* p, int64_t count);
@@ -92,10 +93,13 @@ struct FlatShard {
   void* xb = nullptr;      // bf16 rows, stride ldb (a multiple of 64), zero padded
   int64_t n = 0, cap = 0;
   int* flag = nullptr;     // [0] lo plane nonzero, [1] some value inexact in bf16,
-                           // [2] max squared norm (bits); written by appends
+                           // [2] max squared norm, [3] max ||x - bf16(x)||,
+                           // [4] max ||x - tf32_hi(x)|| (float bits); written by appends
   bool lo_nonzero = false;
   bool bf_inexact = false;
   float max_norm_sq = 0.f;
+  float bf_resid = 0.f;    // upper bounds on the rows' largest representation errors
+  float tf_resid = 0.f;
   cudaEvent_t ev_start = nullptr, ev_stop = nullptr;  // brackets the dominant kernel when profiling
   cudaEvent_t ev_done = nullptr;  // this shard's results are in the gather buffer (own device)
   int last_path = 0, last_fallback = 0, last_refined = 0, last_launches = 0, last_pass = -1;
@@ -182,5 +186,7 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
 px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int metric,
                           const float* d_q, int64_t nq, int k, const uint8_t* d_mask,
                           cudaStream_t stream, void* ws = nullptr);
+px_status first_pass_candidates(const px_flat* h, FlatShard& sh, int metric, const float* d_q, int64_t nq,
+                                int k, cudaStream_t stream, const uint64_t** merged, int* cands, int* pass);
 
 }  // namespace px

@@ -288,12 +288,11 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
   r.ld = h->ld;
   r.d = h->dim;
   r.l2 = l2;
-  r.max_norm = std::sqrt(sh.max_norm_sq);
+  r.max_norm_sq = sh.max_norm_sq;
+  r.x_resid = kind == kPassBf16 ? sh.bf_resid : (kind == kPassTf32 ? sh.tf_resid : 0.f);
   r.x_lo_nonzero = sh.lo_nonzero ? 1 : 0;
   r.q_lo_flag = w.counters + 1;
   r.pass_kind = kind;
-  r.x_bf_inexact = sh.bf_inexact ? 1 : 0;
-  r.q_bf_flag = w.counters + 3;
   r.norm_folded = folded ? 1 : 0;
   r.out = w.final_cands;
   r.status = w.status;
@@ -391,6 +390,35 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
     }
   }
   sh.last_launches = static_cast<int>(g_launches.load() - launches0);
+  return PX_OK;
+}
+
+// Instrumentation: the first tensor-core candidate pass alone (query
+// conversion, K1, split merge; the rescoring runs too but its results are
+// not used). Leaves each query's merged approximate candidates in *merged
+// ([nq][*cands], sorted by approximate key) inside the shard's workspace.
+px_status first_pass_candidates(const px_flat* h, FlatShard& sh, int metric, const float* d_q, int64_t nq,
+                                int k, cudaStream_t stream, const uint64_t** merged, int* cands, int* pass) {
+  if (gemm_cap_for(k) <= 0 || h->ld % 32 != 0 || sh.hl == nullptr || sh.n < 1)
+    return set_error(PX_EUNSUPPORTED, "the tensor-core path cannot serve this request (k or an empty shard)");
+  if (nq > (int64_t(1) << 30)) return set_error(PX_EUNSUPPORTED, "too many queries in one call");
+  const PassKind kind = first_pass_for(h, k);
+  SearchPlan plan;
+  plan_gemm(sh, nq, k, kind, plan);
+  Carver c;
+  TensorWs w;
+  carve_tensor_ws(c, plan, nq, h->ld, h->ldb, k, kind, w);
+  cudaError_t e = sh.ws.reserve(c.used);
+  if (e != cudaSuccess) return cuda_status(e, "search workspace allocation");
+  c = Carver(sh.ws.ptr);
+  carve_tensor_ws(c, plan, nq, h->ld, h->ldb, k, kind, w);
+  int n_fail = 0;
+  bool inexact = false;
+  px_status s = tensor_pass(h, sh, plan, metric, d_q, nq, k, nullptr, kind, w, false, stream, &n_fail, &inexact);
+  if (s != PX_OK) return s;
+  *merged = w.merged;
+  *cands = plan.cands;
+  *pass = kind;
   return PX_OK;
 }
 
