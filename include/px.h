@@ -171,10 +171,13 @@ PX_API px_status px_flat_search_device(const px_flat* h, const float* d_queries,
  * device; results equal px_flat_search's (natural distances, ids 0..n-1).
  * Candidate lists live in a fixed 16 MiB device array inside the library
  * (held on every GPU that loads it); requests needing more (roughly
- * nq * k > 1M) are rejected with PX_EUNSUPPORTED. The first call on a device
- * looks up that array's address and should come before any stream capture.
- * Calls share the array: calls that overlap on the GPU race. Runs on
- * `stream` and returns without synchronising. */
+ * nq * k > 1M) are rejected with PX_EUNSUPPORTED, as are a dim and k whose
+ * query row and candidate buffer exceed a block's shared memory (about
+ * dim > 50,000). The array's address is tied to a CUDA context: the first
+ * call in each context (the current one, whether the runtime's primary
+ * context or the caller's own) looks it up and should come before any stream
+ * capture in that context. Calls share the array: calls that overlap on the
+ * GPU race. Runs on `stream` and returns without synchronising. */
 PX_API px_status px_flat_search_noalloc(const float* d_base, int64_t n, int32_t dim, int32_t metric,
                                         const float* d_queries, int64_t nq, int32_t k,
                                         int64_t* d_out_ids, float* d_out_dists, void* stream);

@@ -158,11 +158,10 @@ cudaError_t launch_exact_buf(const ExactScanArgs& a, cudaStream_t stream) {
 
 int exact_max_k() { return 1024 - kRowsPerIter; }
 
-int exact_group_for(int64_t nq) {
-  if (nq <= 1) return 1;
-  if (nq <= 2) return 2;
-  if (nq <= 4) return 4;
-  return 8;
+int exact_group_for(int64_t nq, int k, int d, size_t smem_limit) {
+  int g = nq <= 1 ? 1 : (nq <= 2 ? 2 : (nq <= 4 ? 4 : 8));
+  while (g > 0 && exact_smem_for(g, k, d) > smem_limit) g >>= 1;
+  return g;
 }
 
 size_t exact_smem_for(int group, int k, int d) {

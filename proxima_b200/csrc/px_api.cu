@@ -11,6 +11,7 @@
 // (crates/core/src/flat.rs:72-85, 106-123, 150-172; pq.rs:54-72, 266-309,
 // 361-377; crates/py/src/lib.rs) as status codes instead of panics.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -138,6 +139,18 @@ int device_sm_count(int dev) {
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
     sms = 148;
   return sms;
+}
+
+size_t device_smem_optin(int dev) {
+  static std::atomic<int> cached[64] = {};
+  if (dev >= 0 && dev < 64 && cached[dev].load() > 0) return static_cast<size_t>(cached[dev].load());
+  int v = 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || v <= 0) {
+    cudaGetLastError();
+    v = 48 * 1024;  // the limit every device offers
+  }
+  if (dev >= 0 && dev < 64) cached[dev] = v;
+  return static_cast<size_t>(v);
 }
 
 px_status resolve_devices(const int32_t* devices, int32_t ndev, std::vector<int>& out) {

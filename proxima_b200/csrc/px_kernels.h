@@ -24,7 +24,9 @@ struct ExactScanArgs {
 };
 cudaError_t launch_exact_scan(const ExactScanArgs& a, cudaStream_t stream);
 int exact_max_k();
-int exact_group_for(int64_t nq);
+// Queries per CTA for nq queries: 1, 2, 4 or 8, the largest whose shared
+// memory (exact_smem_for) fits smem_limit bytes; 0 when even one does not.
+int exact_group_for(int64_t nq, int k, int d, size_t smem_limit);
 int exact_buf_for(int k);
 size_t exact_smem_for(int group, int k, int d);
 

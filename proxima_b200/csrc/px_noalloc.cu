@@ -12,10 +12,14 @@
 // The array: kScratchBytes (16 MiB) of file-scope device memory. Every GPU on
 // which the library is loaded holds it until the process exits. Host code may
 // not use `g_noalloc_scratch` as a device address (on the host the name is a
-// stand-in); the first call on each device resolves the real address with
-// cudaGetSymbolAddress while that device is current, checks the result and
-// caches it, so the first call on a device should be made before any stream
-// capture begins. Every call shares the array and it keeps the previous
+// stand-in). Its device address belongs to one CUDA context: a host program
+// may bind its own driver-API contexts, hold several on one device, or reset
+// a device, and an address resolved in another context would point at
+// invalid memory. So the first call in each context (told apart by the
+// driver's unique context id, which is never reused) resolves the address
+// with cudaGetSymbolAddress while that context is current, checks the result
+// and caches it under that id; that first call should come before any stream
+// capture in the context. Every call shares the array and it keeps the previous
 // call's contents: the call clears the part that must start at zero (its id
 // segment table), and the scan overwrites the rest. Two calls whose work
 // overlaps on the GPU (concurrent streams, or threads on the same device)
@@ -24,11 +28,16 @@
 // Limits: nq * (ncta + 1) * k * 8 bytes of candidate lists must fit in the
 // array (the number of row splits ncta shrinks to make it fit; a request that
 // does not fit even with one split is rejected), dim must be a multiple of 4
-// and the base 16-byte aligned (the scan reads rows with 128-bit loads), and
-// n < 2^32.
+// and the base 16-byte aligned (the scan reads rows with 128-bit loads),
+// n < 2^32, and one query's row plus its candidate buffer must fit in a
+// block's shared memory (about dim <= 50,000 at k <= 768 on B200).
 #include <algorithm>
 #include <mutex>
 #include <string>
+#include <utility>
+#include <vector>
+
+#include <cuda.h>
 
 #include "../../include/px.h"
 #include "px_common.cuh"
@@ -42,25 +51,79 @@ constexpr size_t kSegBytes = 256;  // zeroed (local_begin, global_begin) table
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
+// The driver's current context and its process-unique id, through the
+// runtime's driver entry points (the library links no libcuda).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
 
-px_status scratch_for_current_device(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return px::cuda_status(e, "cudaGetDevice");
-  if (dev < 0 || dev >= kMaxDevices) return px::set_error(PX_EUNSUPPORTED, "device ordinal too large");
-  std::lock_guard<std::mutex> lk(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
+struct CtxFns {
+  CtxGetCurrentFn get_current = nullptr;
+  CtxGetIdFn get_id = nullptr;
+};
+
+const CtxFns& ctx_fns() {
+  static const CtxFns fns = [] {
+    CtxFns f;
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr)
-      return px::cuda_status(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
-                             "cudaGetSymbolAddress(no-allocation scratch)");
-    g_scratch_addr[dev] = p;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      f.get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      f.get_id = reinterpret_cast<CtxGetIdFn>(p);
+    cudaGetLastError();
+    return f;
+  }();
+  return fns;
+}
+
+// Id of the current context, or 0 when there is none yet or it cannot be read.
+unsigned long long current_ctx_id() {
+  const CtxFns& f = ctx_fns();
+  if (!f.get_current || !f.get_id) return 0;
+  CUcontext ctx = nullptr;
+  if (f.get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  if (f.get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+constexpr size_t kMaxContexts = 64;
+std::mutex g_scratch_mu;
+std::vector<std::pair<unsigned long long, void*>> g_scratch_addr;  // (context id, address), newest last
+
+px_status lookup_scratch(void** out) {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr)
+    return px::cuda_status(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
+                           "cudaGetSymbolAddress(no-allocation scratch)");
+  *out = p;
+  return PX_OK;
+}
+
+// The scratch array's device address in the current context.
+px_status scratch_for_current_context(void** out) {
+  unsigned long long id = current_ctx_id();
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (id != 0) {
+    for (const auto& kv : g_scratch_addr)
+      if (kv.first == id) {
+        *out = kv.second;
+        return PX_OK;
+      }
   }
-  *out = g_scratch_addr[dev];
+  // Not seen before, or no context bound yet: the runtime binds the device's
+  // primary context during this lookup.
+  px_status s = lookup_scratch(out);
+  if (s != PX_OK) return s;
+  if (id == 0) id = current_ctx_id();
+  if (id != 0) {
+    if (g_scratch_addr.size() >= kMaxContexts) g_scratch_addr.erase(g_scratch_addr.begin());
+    g_scratch_addr.emplace_back(id, *out);
+  }
   return PX_OK;
 }
 
@@ -90,7 +153,10 @@ extern "C" PX_API px_status px_flat_search_noalloc(const float* d_base, int64_t 
   int sms = 148;
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) sms = px::device_sm_count(dev);
-  const int group = px::exact_group_for(nq);
+  const int group = px::exact_group_for(nq, k, dim, px::device_smem_optin(dev));
+  if (group == 0)
+    return set_error(PX_EUNSUPPORTED, "dim=" + std::to_string(dim) + " with k=" + std::to_string(k) +
+                                          " exceeds the exact scan's shared memory");
   const int64_t groups = (nq + group - 1) / group;
   if (groups > 65535) return set_error(PX_EUNSUPPORTED, "too many queries in one call");
   const int64_t rows_total = n > 0 ? n : 1;
@@ -106,7 +172,7 @@ extern "C" PX_API px_status px_flat_search_noalloc(const float* d_base, int64_t 
   ncta = (rows_total + rows - 1) / rows;
 
   void* base = nullptr;
-  px_status s = scratch_for_current_device(&base);
+  px_status s = scratch_for_current_context(&base);
   if (s != PX_OK) return s;
   unsigned char* scratch = static_cast<unsigned char*>(base);
   int64_t* seg = reinterpret_cast<int64_t*>(scratch);

@@ -20,6 +20,7 @@ px_status set_error(px_status s, const std::string& msg);
 px_status cuda_status(cudaError_t e, const char* what);
 bool all_finite(const float* p, int64_t count);
 int device_sm_count(int dev);
+size_t device_smem_optin(int dev);  // opt-in shared memory per block (bytes)
 px_status resolve_devices(const int32_t* devices, int32_t ndev, std::vector<int>& out);
 void split_rows(int64_t n, int parts, std::vector<int64_t>& begin, std::vector<int64_t>& count);
 

@@ -13,6 +13,7 @@
 #include <atomic>
 #include <cmath>
 #include <numeric>
+#include <string>
 #include <vector>
 
 #include "px_common.cuh"
@@ -147,7 +148,10 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
     if (masked) c.take(sizeof(uint32_t) * mask_words(sh.n));
   } else {
     plan.path = FlatPath::Exact;
-    const int group = exact_group_for(nq);
+    const int group = exact_group_for(nq, k, h->dim, device_smem_optin(sh.device));
+    if (group == 0)
+      return set_error(PX_EUNSUPPORTED, "dim=" + std::to_string(h->dim) + " with k=" + std::to_string(k) +
+                                            " exceeds the exact scan's shared memory");
     const int64_t groups = (nq + group - 1) / group;
     if (groups > 65535) return set_error(PX_EUNSUPPORTED, "too many queries in one call");
     const int64_t target = static_cast<int64_t>(sh.sms) * 4;
@@ -200,7 +204,10 @@ static px_status run_exact(const px_flat* h, FlatShard& sh, int metric, const fl
 static px_status exact_for_list(const px_flat* h, FlatShard& sh, int metric, const float* src_q,
                                 const int* idx, int count, int k, const uint8_t* d_mask,
                                 uint64_t* dst, cudaStream_t stream) {
-  const int group = exact_group_for(count);
+  const int group = exact_group_for(count, k, h->dim, device_smem_optin(sh.device));
+  if (group == 0)
+    return set_error(PX_EUNSUPPORTED, "dim=" + std::to_string(h->dim) + " with k=" + std::to_string(k) +
+                                          " exceeds the exact scan's shared memory");
   const int64_t groups = (count + group - 1) / group;
   const int64_t n = std::max<int64_t>(sh.n, 1);
   int64_t ncta = std::max<int64_t>(1, (static_cast<int64_t>(sh.sms) * 4 + groups - 1) / groups);
