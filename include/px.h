@@ -204,6 +204,17 @@ PX_API px_status px_merge_shards_device(int32_t device, const float* d_keys, con
                                         int32_t natural, float* d_out_dists, int64_t* d_out_ids,
                                         void* stream);
 
+/* The same merge over shard RECORDS, the layout one collective moves: record
+ * g (px_shard_record_bytes(nq, k) bytes, records back to back, 16-byte
+ * aligned) holds shard g's ids [nq][k] (int64) followed by its keys [nq][k]
+ * (float). A rank writes its record with px_flat_search_device (key_space =
+ * 1, ids at the record's start, keys 8*nq*k bytes in), and one all-gather of
+ * the records brings every shard's lists to every rank. */
+PX_API int64_t px_shard_record_bytes(int64_t nq, int32_t k);
+PX_API px_status px_merge_shard_records_device(int32_t device, const void* d_records, int32_t nshard, int64_t nq,
+                                               int32_t k, int32_t metric, int32_t natural, float* d_out_dists,
+                                               int64_t* d_out_ids, void* stream);
+
 /* ------------------------------------------------------------------------
  * PqIndex (crates/core/src/pq.rs) on one or more GPUs.
  * ------------------------------------------------------------------------ */

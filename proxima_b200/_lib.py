@@ -77,6 +77,8 @@ SIGNATURES = {
     "px_flat_search_noalloc": (_i32, [_vp, _i64, _i32, _i32, _vp, _i64, _i32, _vp, _vp, _vp]),
     "px_flat_debug_candidates": (_i32, [_vp, _f32p, _i64, _i32, _i32, _i64p, _f32p, _i32p, _i32p]),
     "px_merge_shards_device": (_i32, [_i32, _vp, _vp, _i32, _i64, _i32, _i32, _i32, _vp, _vp, _vp]),
+    "px_shard_record_bytes": (_i64, [_i64, _i32]),
+    "px_merge_shard_records_device": (_i32, [_i32, _vp, _i32, _i64, _i32, _i32, _i32, _vp, _vp, _vp]),
     "px_pq_train": (_i32, [_f32p, _i64, _i32, _i32, _i32, _i32, _i64, _u64, _i32, _f32p]),
     "px_pq_create": (_i32, [_i32, _i32, _i32, _i32, _f32p, _i32p, _i32, _c.POINTER(_vp)]),
     "px_pq_destroy": (_i32, [_vp]),

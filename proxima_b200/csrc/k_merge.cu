@@ -102,24 +102,25 @@ __global__ void emit_kernel(const uint64_t* __restrict__ cands, int64_t total, b
 }
 
 // One thread per query: G-way merge of per-shard sorted (key, id) lists.
-__global__ void merge_shards_kernel(const float* __restrict__ keys, const int64_t* __restrict__ ids,
+// Shard g's lists start key_stride / id_stride bytes after shard g-1's.
+__global__ void merge_shards_kernel(const char* __restrict__ keys, int64_t key_stride,
+                                    const char* __restrict__ ids, int64_t id_stride,
                                     int nshard, int64_t nq, int k, bool l2, bool natural,
                                     float* __restrict__ out_dists, int64_t* __restrict__ out_ids) {
   int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (q >= nq) return;
   int pos[8];
   for (int g = 0; g < nshard; ++g) pos[g] = 0;
-  const int64_t stride = nq * k;
   for (int j = 0; j < k; ++j) {
     int win = -1;
     uint32_t wk = 0;
     int64_t wid = 0;
     for (int g = 0; g < nshard; ++g) {
       if (pos[g] >= k) continue;
-      int64_t e = g * stride + q * k + pos[g];
-      int64_t id = ids[e];
+      const int64_t e = q * k + pos[g];
+      const int64_t id = reinterpret_cast<const int64_t*>(ids + g * id_stride)[e];
       if (id < 0) continue;
-      uint32_t o = key_to_ord(keys[e]);
+      const uint32_t o = key_to_ord(reinterpret_cast<const float*>(keys + g * key_stride)[e]);
       if (win < 0 || o < wk || (o == wk && id < wid)) {
         win = g;
         wk = o;
@@ -166,11 +167,20 @@ cudaError_t launch_emit(const uint64_t* cands, int64_t nq, int k, bool l2, bool 
 cudaError_t launch_merge_shards(const float* keys, const int64_t* ids, int nshard, int64_t nq, int k,
                                 bool l2, bool natural, float* out_dists, int64_t* out_ids,
                                 cudaStream_t stream) {
+  return launch_merge_shards_strided(keys, static_cast<int64_t>(sizeof(float)) * nq * k, ids,
+                                     static_cast<int64_t>(sizeof(int64_t)) * nq * k, nshard, nq, k, l2, natural,
+                                     out_dists, out_ids, stream);
+}
+
+cudaError_t launch_merge_shards_strided(const float* keys, int64_t key_stride, const int64_t* ids,
+                                        int64_t id_stride, int nshard, int64_t nq, int k, bool l2, bool natural,
+                                        float* out_dists, int64_t* out_ids, cudaStream_t stream) {
   if (nq == 0 || k == 0) return cudaSuccess;
   if (nshard < 1 || nshard > 8) return cudaErrorInvalidValue;
   const int threads = 128;
   merge_shards_kernel<<<static_cast<unsigned>((nq + threads - 1) / threads), threads, 0, stream>>>(
-      keys, ids, nshard, nq, k, l2, natural, out_dists, out_ids);
+      reinterpret_cast<const char*>(keys), key_stride, reinterpret_cast<const char*>(ids), id_stride, nshard, nq,
+      k, l2, natural, out_dists, out_ids);
   return cudaGetLastError();
 }
 

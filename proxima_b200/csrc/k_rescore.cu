@@ -98,15 +98,75 @@ rescore_kernel(const RescoreArgs a) {
   }
   __syncwarp();
 
-  // Exact keys, four candidates at a time: thread l of a group of eight runs
-  // the reference's lane-l accumulator (acc_l += term(x[8c + l], q[8c + l]),
-  // c = 0, 1, ...) on its own, so each accumulator is the same sequential
-  // chain as the reference's, and the group reads 32 contiguous bytes of the
-  // row per step. The lanes are then summed left to right and the remainder
-  // added, as distance.rs does.
+  // The certificate's bound. lower_bound(a) is, in the reference's key space,
+  // a lower bound on the exact key of every row whose approximate key is >= a
+  // (eps as in the header; increasing in a).
+  const double ref = (a.d / 8 + 10) * 0x1p-23;  // the reference's relative rounding
+  const double qn = sqrt(qsq) * (1.0 + 0x1p-40);
+  // Upper bound on every row's real norm: the shard keeps the largest fp32
+  // norm, itself rounded in the reference's order.
+  const double xn2 = static_cast<double>(a.max_norm_sq) * (1.0 + ref);
+  const double xn = sqrt(xn2) * (1.0 + 0x1p-40);
+  const double S = qn * xn;
+  const bool q_lo = *a.q_lo_flag != 0;
+  int npass = 1;
+  double e_rep = 0.0;  // bound on |q'.x - (the pass's product of the rounded copies)|
+  if (a.pass_kind == kPassBf16 || a.pass_kind == kPassTf32) {
+    e_rep = (sqrt(rq2) * xn + sqrt(qt2) * static_cast<double>(a.x_resid)) * (1.0 + 0x1p-40);
+  } else if (q_lo || a.x_lo_nonzero) {
+    npass = 1 + (q_lo ? 1 : 0) + (a.x_lo_nonzero ? 1 : 0);
+    e_rep = 4.0 * 0x1p-22 * S;
+  }
+  const int dk = folded ? a.d + 3 : a.d;  // K values with nonzero products
+  const double products = static_cast<double>(npass) * dk + 2.0;
+  const double M = folded ? 2.02 * S + xn2 : 1.01 * S;
+  const double e_acc = 3.0 * 0x1p-23 * products * M + products * (1.0 + qn + xn) * 0x1p-120;
+  const double qn2 = qn * qn;
+  // Folded L2: the pass's key is -(2q~.x~ - ||x||^2) and e_rep already bounds
+  // the doubled product; other L2 passes compute ||x||^2 - 2 q~.x~.
+  const double e_fixed = L2 ? (folded ? e_rep + e_acc : 2.0 * (e_rep + e_acc)) + xn2 * ref +
+                                  (qn + xn) * (qn + xn) * ref
+                            : e_rep + e_acc + S * ref;
+  const bool in_range = S < 0x1p100 && xn2 < 0x1p100;
+  auto lower_bound = [&](double akey) {
+    return L2 ? akey + qn2 - (e_fixed + (fabs(akey) + qn2) * 0x1p-22) : akey - (e_fixed + fabs(akey) * 0x1p-22);
+  };
+
+  // Every row outside the candidate set has an approximate key >=
+  // min(A_cap, max of every full split list): when the per-split lists are
+  // shorter than the merged set, a split can hide rows below A_cap.
   const uint64_t* mq = a.merged + q * a.cap;
+  uint64_t last = mq[a.cap - 1];
+  if (a.list_cap < a.cap) {
+    uint64_t m = PX_EMPTY;
+    const uint64_t* ql = a.lists + q * static_cast<int64_t>(a.nlists) * a.list_cap;
+    for (int j = lane; j < a.nlists; j += 32) {
+      const uint64_t lmax = ql[static_cast<int64_t>(j) * a.list_cap + a.list_cap - 1];
+      m = lmax < m ? lmax : m;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const uint64_t o = __shfl_xor_sync(0xffffffffu, m, off);
+      m = o < m ? o : m;
+    }
+    last = m < last ? m : last;
+  }
+
+  // Exact keys, four candidates at a time, in approximate-key order: thread l
+  // of a group of eight runs the reference's lane-l accumulator
+  // (acc_l += term(x[8c + l], q[8c + l]), c = 0, 1, ...) on its own, so each
+  // accumulator is the same sequential chain as the reference's, and the
+  // group reads 32 contiguous bytes of the row per step. The lanes are then
+  // summed left to right and the remainder added, as distance.rs does.
+  // Early exit: once `done` candidates are scored, every unscored candidate
+  // and every row outside the set has an approximate key >= a* = min(the
+  // next candidate's, last), hence an exact key >= lower_bound(a*). If k
+  // scored keys lie strictly below that, no other row can reach the top k
+  // (not even tie), so the top k of the scored ones is the answer, certified.
   const int grp = lane >> 3, l = lane & 7, g0 = lane & ~7;
   const int chunks = a.d >> 3;
+  int scored = a.cap;
+  bool early = false;
   for (int j0 = 0; j0 < a.cap; j0 += 4) {
     const int j = j0 + grp;
     const uint64_t c = j < a.cap ? mq[j] : PX_EMPTY;
@@ -129,13 +189,33 @@ rescore_kernel(const RescoreArgs a) {
       }
       s_c[j] = e;
     }
+    __syncwarp();
+    const int done = j0 + 4;
+    if (done >= a.k && done < a.cap && in_range) {
+      const uint64_t next = mq[done];
+      if (next == PX_EMPTY) {  // the rest of the merged list is empty
+        scored = done;
+        break;
+      }
+      const uint64_t astar = next < last ? next : last;
+      const double T = lower_bound(static_cast<double>(cand_key(astar)));
+      int below = 0;
+      for (int i = lane; i < done; i += 32)
+        below += (s_c[i] != PX_EMPTY && static_cast<double>(cand_key(s_c[i])) < T) ? 1 : 0;
+      if (__reduce_add_sync(0xffffffffu, below) >= a.k) {
+        scored = done;
+        early = true;
+        break;
+      }
+    }
   }
   __syncwarp();
-  // Rank sort (values are distinct except PX_EMPTY; equal ones rank by index).
-  for (int j = lane; j < a.cap; j += 32) {
+  // Rank sort of the scored candidates (values are distinct except PX_EMPTY;
+  // equal ones rank by index).
+  for (int j = lane; j < scored; j += 32) {
     const uint64_t v = s_c[j];
     int rank = 0;
-    for (int i = 0; i < a.cap; ++i) {
+    for (int i = 0; i < scored; ++i) {
       const uint64_t u = s_c[i];
       rank += (u < v) || (u == v && i < j);
     }
@@ -143,65 +223,16 @@ rescore_kernel(const RescoreArgs a) {
   }
   __syncwarp();
 
-  // Certificate. Every row outside the candidate set has an approximate key
-  // >= min(A_cap, max of every full split list): when the per-split lists
-  // are shorter than the merged set, a split can hide rows below A_cap.
   int ok = 1;
-  uint64_t last = mq[a.cap - 1];
-  if (a.list_cap < a.cap) {
-    uint64_t m = PX_EMPTY;
-    const uint64_t* ql = a.lists + q * static_cast<int64_t>(a.nlists) * a.list_cap;
-    for (int j = lane; j < a.nlists; j += 32) {
-      const uint64_t lmax = ql[static_cast<int64_t>(j) * a.list_cap + a.list_cap - 1];
-      m = lmax < m ? lmax : m;
+  if (!early) {
+    const uint64_t kth = s_sorted[a.k - 1];
+    if (last != PX_EMPTY && kth == PX_EMPTY) {
+      // Fewer than k candidates, yet a full list may hide rows: not certified.
+      ok = 0;
+    } else if (last != PX_EMPTY) {
+      const double bound = lower_bound(static_cast<double>(cand_key(last)));
+      ok = (static_cast<double>(cand_key(kth)) < bound && in_range) ? 1 : 0;
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const uint64_t o = __shfl_xor_sync(0xffffffffu, m, off);
-      m = o < m ? o : m;
-    }
-    last = m < last ? m : last;
-  }
-  const uint64_t kth = s_sorted[a.k - 1];
-  if (last != PX_EMPTY && kth == PX_EMPTY) {
-    // Fewer than k candidates, yet a full list may hide rows: not certified.
-    ok = 0;
-  } else if (last != PX_EMPTY) {
-    const double ref = (a.d / 8 + 10) * 0x1p-23;  // the reference's relative rounding
-    const double qn = sqrt(qsq) * (1.0 + 0x1p-40);
-    // Upper bound on every row's real norm: the shard keeps the largest fp32
-    // norm, itself rounded in the reference's order.
-    const double xn2 = static_cast<double>(a.max_norm_sq) * (1.0 + ref);
-    const double xn = sqrt(xn2) * (1.0 + 0x1p-40);
-    const double S = qn * xn;
-    const bool q_lo = *a.q_lo_flag != 0;
-    int npass = 1;
-    double e_rep = 0.0;  // bound on |q'.x - (the pass's product of the rounded copies)|
-    if (a.pass_kind == kPassBf16 || a.pass_kind == kPassTf32) {
-      e_rep = (sqrt(rq2) * xn + sqrt(qt2) * static_cast<double>(a.x_resid)) * (1.0 + 0x1p-40);
-    } else if (q_lo || a.x_lo_nonzero) {
-      npass = 1 + (q_lo ? 1 : 0) + (a.x_lo_nonzero ? 1 : 0);
-      e_rep = 4.0 * 0x1p-22 * S;
-    }
-    const int dk = folded ? a.d + 3 : a.d;  // K values with nonzero products
-    const double products = static_cast<double>(npass) * dk + 2.0;
-    const double M = folded ? 2.02 * S + xn2 : 1.01 * S;
-    const double e_acc = 3.0 * 0x1p-23 * products * M + products * (1.0 + qn + xn) * 0x1p-120;
-    const double A = static_cast<double>(cand_key(last));
-    const double Ek = static_cast<double>(cand_key(kth));
-    double bound;
-    if (L2) {
-      // Folded: the pass's key is -(2q~.x~ - ||x||^2) and e_rep already
-      // bounds the doubled product; otherwise ||x||^2 - 2 q~.x~.
-      const double qn2 = qn * qn;
-      const double e_key = folded ? e_rep + e_acc : 2.0 * (e_rep + e_acc);
-      const double eps = e_key + xn2 * ref + (qn + xn) * (qn + xn) * ref + (fabs(A) + qn2) * 0x1p-22;
-      bound = A + qn2 - eps;
-    } else {
-      const double eps = e_rep + e_acc + S * ref + fabs(A) * 0x1p-22;
-      bound = A - eps;
-    }
-    ok = (Ek < bound && S < 0x1p100 && xn2 < 0x1p100) ? 1 : 0;
   }
   for (int j = lane; j < a.k; j += 32) a.out[q * a.k + j] = s_sorted[j];
   if (lane == 0) {

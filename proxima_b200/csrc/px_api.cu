@@ -961,6 +961,32 @@ PX_API px_status px_merge_shards_device(int32_t device, const float* d_keys, con
   return cuda_status(e, "merge_shards launch");
 }
 
+PX_API int64_t px_shard_record_bytes(int64_t nq, int32_t k) {
+  if (nq < 0 || k < 0) return 0;
+  return (nq * k * 12 + 15) / 16 * 16;
+}
+
+PX_API px_status px_merge_shard_records_device(int32_t device, const void* d_records, int32_t nshard, int64_t nq,
+                                               int32_t k, int32_t metric, int32_t natural, float* d_out_dists,
+                                               int64_t* d_out_ids, void* stream) {
+  if (nshard < 1 || nshard > 8) return set_error(PX_EINVAL, "nshard must be in 1..=8");
+  if (k < 0 || nq < 0) return set_error(PX_EINVAL, "negative size");
+  if (metric != PX_METRIC_L2 && metric != PX_METRIC_IP) return set_error(PX_EINVAL, "bad metric");
+  if (nq == 0 || k == 0) return PX_OK;
+  if (d_records == nullptr || d_out_dists == nullptr || d_out_ids == nullptr)
+    return set_error(PX_EINVAL, "null buffer");
+  if (reinterpret_cast<uintptr_t>(d_records) % 16 != 0)
+    return set_error(PX_EINVAL, "records must be 16-byte aligned");
+  const int64_t rec = px_shard_record_bytes(nq, k);
+  const char* base = static_cast<const char*>(d_records);
+  DeviceGuard dg(device);
+  cudaError_t e = launch_merge_shards_strided(reinterpret_cast<const float*>(base + 8 * nq * k), rec,
+                                              reinterpret_cast<const int64_t*>(base), rec, nshard, nq, k,
+                                              metric == PX_METRIC_L2, natural != 0, d_out_dists, d_out_ids,
+                                              static_cast<cudaStream_t>(stream));
+  return cuda_status(e, "merge_shards launch");
+}
+
 // ---- reference-compatible ABI (knn.cu:123-180) ----------------------------
 
 struct PxGpuIndex {

@@ -57,6 +57,12 @@ cudaError_t launch_emit(const uint64_t* cands, int64_t nq, int k, bool l2, bool 
 cudaError_t launch_merge_shards(const float* keys, const int64_t* ids, int nshard, int64_t nq,
                                 int k, bool l2, bool natural, float* out_dists, int64_t* out_ids,
                                 cudaStream_t stream);
+// The same with shard g's keys at (char*)keys + g * key_stride and its ids at
+// (char*)ids + g * id_stride (byte strides), e.g. records gathered by one
+// collective.
+cudaError_t launch_merge_shards_strided(const float* keys, int64_t key_stride, const int64_t* ids,
+                                        int64_t id_stride, int nshard, int64_t nq, int k, bool l2, bool natural,
+                                        float* out_dists, int64_t* out_ids, cudaStream_t stream);
 
 // ---- PQ (k_pq.cu) ---------------------------------------------------------
 // ADC tables (pq.rs:123-136): lut [nq][m][ksub].

@@ -3,10 +3,10 @@
 Each rank holds a contiguous run of base rows [offset, offset + n_local) in a
 single-device ``px_flat`` handle. A search runs every rank's local top-k on
 its GPU (key space: squared L2 or negated inner product, sorted, ties by
-global id), gathers the per-rank lists with one NCCL all-gather over
-NVLink, and merges them on the device (``px_merge_shards_device``). Every
-rank ends up with the same final top-k, identical to a single index holding
-all rows.
+global id) straight into one record buffer (ids, then keys), gathers the
+records with a single NCCL all-gather over NVLink, and merges them on the
+device (``px_merge_shard_records_device``). Every rank ends up with the same
+final top-k, identical to a single index holding all rows.
 
 torch.distributed provides the process group and NCCL; torch tensors hold
 the device buffers. The search itself is libproxima_b200's kernels.
@@ -73,12 +73,13 @@ class ShardedFlatIndex:
         key = (nq, k)
         if key not in self._bufs:
             dev = self.device
+            rec = int(self._lib.px_shard_record_bytes(nq, k))
             self._bufs = {key: dict(
-                ids=torch.empty((nq, k), dtype=torch.int64, device=dev),
-                keys=torch.empty((nq, k), dtype=torch.float32, device=dev),
-                # rank lists concatenated on dim 0: [world * nq, k] == [world][nq][k]
-                all_ids=torch.empty((self.world * nq, k), dtype=torch.int64, device=dev),
-                all_keys=torch.empty((self.world * nq, k), dtype=torch.float32, device=dev),
+                rec=rec,
+                # this rank's record: ids [nq][k] int64, then keys [nq][k] float32
+                record=torch.empty(rec, dtype=torch.uint8, device=dev),
+                # every rank's record, back to back (rank order)
+                records=torch.empty(self.world * rec, dtype=torch.uint8, device=dev),
                 out_ids=torch.empty((nq, k), dtype=torch.int64, device=dev),
                 out_d=torch.empty((nq, k), dtype=torch.float32, device=dev),
             )}
@@ -92,19 +93,20 @@ class ShardedFlatIndex:
         b = self._buffers(nq, k)
         stream = torch.cuda.current_stream(self.device)
         sp = ctypes.c_void_p(stream.cuda_stream)
-        single = self.world == 1
-        _lib.check(self._lib.px_flat_search_device(
-            self.local.handle, ctypes.c_void_p(queries.data_ptr()), nq, k, 0 if single else 1,
-            ctypes.c_void_p((b["out_ids"] if single else b["ids"]).data_ptr()),
-            ctypes.c_void_p((b["out_d"] if single else b["keys"]).data_ptr()), sp))
-        if single:
+        if self.world == 1:
+            _lib.check(self._lib.px_flat_search_device(
+                self.local.handle, ctypes.c_void_p(queries.data_ptr()), nq, k, 0,
+                ctypes.c_void_p(b["out_ids"].data_ptr()), ctypes.c_void_p(b["out_d"].data_ptr()), sp))
             return b["out_ids"], b["out_d"]
-        dist.all_gather_into_tensor(b["all_keys"], b["keys"], group=self.group)
-        dist.all_gather_into_tensor(b["all_ids"], b["ids"], group=self.group)
-        _lib.check(self._lib.px_merge_shards_device(
-            self.device.index, ctypes.c_void_p(b["all_keys"].data_ptr()),
-            ctypes.c_void_p(b["all_ids"].data_ptr()), self.world, nq, k, int(self.metric), 1,
-            ctypes.c_void_p(b["out_d"].data_ptr()), ctypes.c_void_p(b["out_ids"].data_ptr()), sp))
+        rec = b["record"].data_ptr()
+        _lib.check(self._lib.px_flat_search_device(
+            self.local.handle, ctypes.c_void_p(queries.data_ptr()), nq, k, 1,
+            ctypes.c_void_p(rec), ctypes.c_void_p(rec + 8 * nq * k), sp))
+        dist.all_gather_into_tensor(b["records"], b["record"], group=self.group)
+        _lib.check(self._lib.px_merge_shard_records_device(
+            self.device.index, ctypes.c_void_p(b["records"].data_ptr()), self.world, nq, k,
+            int(self.metric), 1, ctypes.c_void_p(b["out_d"].data_ptr()),
+            ctypes.c_void_p(b["out_ids"].data_ptr()), sp))
         return b["out_ids"], b["out_d"]
 
     def search_batch(self, queries: np.ndarray, k: int = 10):

@@ -1,11 +1,13 @@
 """Row-sharded search across processes.
 
 CPU (gloo, world size 2): the sharding scheme of proxima_b200.distributed --
-contiguous shard ranges, global ids by offset, one all-gather of the per-rank
-key-space top-k lists, merge by (key, global id) -- reproduces a single
+contiguous shard ranges, global ids by offset, each rank's key-space top-k
+packed into one record (ids then keys, px_shard_record_bytes long), one
+all-gather of the records, merge by (key, global id) -- reproduces a single
 index's top-k (tie-aware rule). Each rank's local lists come from the CPU
-oracle here, since the CPU box has no GPU; the collective shapes and dtypes
-are the ones ShardedFlatIndex uses.
+oracle here, since the CPU box has no GPU; the record layout, the collective
+and its dtype are the ones ShardedFlatIndex uses. (The merge kernel itself
+is tested on one GPU in tests/test_merge_gpu.py.)
 
 GPU (NCCL, 2 GPUs, skipped with fewer): ShardedFlatIndex end to end against
 the oracle on the full base.
@@ -21,6 +23,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle as O
+from proxima_b200 import _lib
 from proxima_b200.distributed import shard_range
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -81,15 +84,19 @@ def _gloo_worker(rank, world, port, metric, result_q):
         lo, hi = shard_range(n, world, rank)
         ids, d = O.flat_search_batch(data[lo:hi], metric, queries, k)
         ids = np.where(ids >= 0, ids + lo, -1)
-        keys = torch.from_numpy(_key_space(data, metric, queries, ids))
-        tids = torch.from_numpy(ids)
-        # Same layout as ShardedFlatIndex: rank lists concatenated on dim 0.
-        all_keys = torch.empty((world * nq, k), dtype=torch.float32)
-        all_ids = torch.empty((world * nq, k), dtype=torch.int64)
-        dist.all_gather_into_tensor(all_keys, keys)
-        dist.all_gather_into_tensor(all_ids, tids)
+        keys = _key_space(data, metric, queries, ids)
+        # Same layout as ShardedFlatIndex: one record per rank, ids then keys.
+        rec = int(_lib.load().px_shard_record_bytes(nq, k))
+        record = np.zeros(rec, np.uint8)
+        record[: 8 * nq * k] = ids.astype(np.int64).reshape(-1).view(np.uint8)
+        record[8 * nq * k: 12 * nq * k] = keys.astype(np.float32).reshape(-1).view(np.uint8)
+        records = torch.empty(world * rec, dtype=torch.uint8)
+        dist.all_gather_into_tensor(records, torch.from_numpy(record))
         if rank == 0:
-            mids, mkeys = _merge(all_keys.view(world, nq, k).numpy(), all_ids.view(world, nq, k).numpy(), k)
+            r = records.numpy().reshape(world, rec)
+            all_ids = r[:, : 8 * nq * k].copy().view(np.int64).reshape(world, nq, k)
+            all_keys = r[:, 8 * nq * k: 12 * nq * k].copy().view(np.float32).reshape(world, nq, k)
+            mids, mkeys = _merge(all_keys, all_ids, k)
             nat = np.where(mids >= 0, np.sqrt(mkeys) if metric == O.L2 else -mkeys, 0).astype(np.float32)
             ref_ids, ref_d = O.flat_search_batch(data, metric, queries, k)
             from tests import _parity
