@@ -246,6 +246,13 @@ PX_API px_status px_pq_read_codes(const px_pq* h, int64_t start, int64_t count, 
 /* As px_flat_last_profile, for the last PQ search (path = 2, the ADC scan). */
 PX_API px_status px_pq_last_profile(const px_pq* h, px_search_profile* out);
 
+/* Device-memory variant of px_pq_search on a single-device handle, as
+ * px_flat_search_device: d_queries (nq x dim) and both outputs on the
+ * handle's device, enqueued on `stream` (NULL: the default stream) without
+ * a host wait; key_space != 0 writes squared-L2 / -IP keys. */
+PX_API px_status px_pq_search_device(const px_pq* h, const float* d_queries, int64_t nq, int32_t k,
+                                     int32_t key_space, int64_t* d_out_ids, float* d_out_dists, void* stream);
+
 /* PqIndex::search_batch (pq.rs:349-396) and its filtered form. */
 PX_API px_status px_pq_search(const px_pq* h, const float* queries, int64_t nq, int32_t k,
                               int64_t* out_ids, float* out_dists);

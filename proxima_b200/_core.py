@@ -282,6 +282,12 @@ class PqIndex:
             self._lib.px_pq_destroy(h)
             self._h = None
 
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        """The px_pq* handle (for callers that drive the C ABI directly);
+        None until the index is trained."""
+        return self._h
+
     # -- lib.rs:472-490 ----------------------------------------------------
     def train(self, training) -> None:
         t = _array(training, 2, np.float32, "training")

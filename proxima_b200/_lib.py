@@ -88,6 +88,7 @@ SIGNATURES = {
     "px_pq_size": (_i64, [_vp]),
     "px_pq_last_profile": (_i32, [_vp, _vp]),
     "px_pq_search": (_i32, [_vp, _f32p, _i64, _i32, _i64p, _f32p]),
+    "px_pq_search_device": (_i32, [_vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp]),
     "px_pq_search_filtered": (_i32, [_vp, _f32p, _i64, _i32, _u8p, _i64p, _f32p]),
 }
 

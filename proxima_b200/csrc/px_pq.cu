@@ -593,6 +593,26 @@ PX_API px_status px_pq_search(const px_pq* h, const float* queries, int64_t nq, 
   return pq_search_host(h, queries, nq, k, nullptr, out_ids, out_dists);
 }
 
+PX_API px_status px_pq_search_device(const px_pq* hc, const float* d_queries, int64_t nq, int32_t k,
+                                     int32_t key_space, int64_t* d_out_ids, float* d_out_dists, void* stream) {
+  px_status s = pq_check(hc);
+  if (s != PX_OK) return s;
+  if (k < 0 || nq < 0) return set_error(PX_EINVAL, "k and nq must be >= 0");
+  if (k > PX_MAX_K)
+    return set_error(PX_EUNSUPPORTED, "k=" + std::to_string(k) + " exceeds PX_MAX_K=" + std::to_string(PX_MAX_K));
+  if (hc->shards.size() != 1)
+    return set_error(PX_EUNSUPPORTED, "px_pq_search_device needs a single-device handle");
+  if (k == 0 || nq == 0) return PX_OK;
+  if (d_queries == nullptr || d_out_ids == nullptr || d_out_dists == nullptr)
+    return set_error(PX_EINVAL, "null buffer");
+  px_pq* h = const_cast<px_pq*>(hc);
+  std::lock_guard<std::mutex> lk(h->mu);
+  PqShard& sh = h->shards[0];
+  DeviceGuard dg(sh.device);
+  return pq_shard_search(h, sh, d_queries, nq, k, nullptr, key_space == 0, d_out_ids, d_out_dists,
+                         static_cast<cudaStream_t>(stream));
+}
+
 PX_API px_status px_pq_search_filtered(const px_pq* h, const float* queries, int64_t nq, int32_t k,
                                        const uint8_t* mask, int64_t* out_ids, float* out_dists) {
   px_status s = pq_check(h);

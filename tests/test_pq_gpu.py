@@ -79,6 +79,41 @@ def test_config3_shape(pxm):
 
 
 @pytest.mark.parametrize("metric", [O.L2, O.IP])
+def test_search_device_matches_host_search(pxm, metric):
+    # px_pq_search_device: queries and results in device memory on the
+    # caller's stream; natural distances equal px_pq_search's bit for bit,
+    # key space is squared L2 / -IP.
+    import ctypes
+
+    import torch
+
+    base, queries = _data.sift_like(20000, 19, seed=11, centres=50)
+    pq = pxm.PqIndex(128, _metric(pxm, metric), m=16, train_iters=4, seed=9)
+    pq.train(base)
+    pq.add(base)
+    k = 10
+    want_ids, want_d = pq.search_batch(queries, k=k)
+    dev = torch.device("cuda", 0)
+    d_q = torch.from_numpy(queries).to(dev)
+    lib = pxm._lib.load()
+    sp = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    for key_space in (0, 1):
+        ids = torch.empty((len(queries), k), dtype=torch.int64, device=dev)
+        d = torch.empty((len(queries), k), dtype=torch.float32, device=dev)
+        pxm._lib.check(lib.px_pq_search_device(pq.handle, ctypes.c_void_p(d_q.data_ptr()), len(queries), k,
+                                               key_space, ctypes.c_void_p(ids.data_ptr()),
+                                               ctypes.c_void_p(d.data_ptr()), sp))
+        torch.cuda.synchronize()
+        got_ids, got_d = ids.cpu().numpy(), d.cpu().numpy()
+        assert np.array_equal(got_ids, want_ids)
+        if key_space == 0:
+            assert np.array_equal(got_d.view(np.uint32), want_d.view(np.uint32))
+        else:
+            nat = np.sqrt(got_d) if metric == O.L2 else -got_d
+            assert np.array_equal(nat.astype(np.float32).view(np.uint32), want_d.view(np.uint32))
+
+
+@pytest.mark.parametrize("metric", [O.L2, O.IP])
 def test_m16_scan_edges(pxm, metric):
     # m = 16 with 256 centroids and 8-query groups is the scan's skewed path:
     # a ragged row count over several CTAs and iterations, a partial last
