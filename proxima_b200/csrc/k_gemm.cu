@@ -469,8 +469,7 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       int maxpos = 0;
       for (int t = t0; t < t1; ++t) {
         // Warp-uniform decision: the tcgen05.ld below is .sync.aligned.
-        // Tiles take microseconds: poll every ~256 ns.
-        const bool got = __all_sync(0xffffffffu, tc::mbar_wait(tfull_bar(acc), acc_phase, s_abort, 256));
+        const bool got = __all_sync(0xffffffffu, tc::mbar_wait(tfull_bar(acc), acc_phase, s_abort));
         if (!got) {
           ok = false;
           break;
@@ -724,7 +723,7 @@ gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       float thr_key = __int_as_float(qidx < p.nq ? 0x7f800000 : 0xff800000);
       int maxpos = 0;
       for (int t = t0; t < t1; ++t) {
-        const bool got = __all_sync(0xffffffffu, tc::mbar_wait(tfull_bar(acc), acc_phase, s_abort, 256));
+        const bool got = __all_sync(0xffffffffu, tc::mbar_wait(tfull_bar(acc), acc_phase, s_abort));
         if (!got) {
           ok = false;
           break;

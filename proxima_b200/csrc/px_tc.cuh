@@ -54,19 +54,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait. Polls the phase and sleeps ~sleep_ns between polls, so a
-// waiting warp takes no issue slots from the warps that do the work; every
-// 64 polls it checks the shared abort flag and the wall-clock limit.
-// Returns false (and raises *abort) on timeout, or false early when another
-// role already raised *abort.
+// try_wait with a suspend-time hint: the thread may be suspended for up to
+// hint_ns and resumes as soon as the phase completes (or the hint runs out),
+// so a waiting warp takes no issue slots and still wakes without delay.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait. Each poll suspends the thread for up to hint_ns (woken early
+// when the phase completes); every 16 polls it checks the shared abort flag
+// and the wall-clock limit. Returns false (and raises *abort) on timeout, or
+// false early when another role already raised *abort.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
-                                          uint32_t sleep_ns = 32) {
+                                          uint32_t hint_ns = 1000) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
-    __nanosleep(sleep_ns);
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63) == 0) {
+    if (mbar_try_wait_hint(bar, parity, hint_ns)) return true;
+    if ((i & 15) == 0) {
       if (*abort) return false;
       if (globaltimer() - t0 > kWaitTimeoutNs) {
         *abort = 1;
