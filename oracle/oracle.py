@@ -255,3 +255,76 @@ def check_topk(metric: int, data, queries, ids, dists, ref_ids, ref_dists, *, fi
                     f"id mismatch at query {q} rank {j} without a tie: {row_ids[j]} vs {ref_ids[q, j]}")
         n_tie += diff.size
     return n_tie
+
+
+# ---- the reference's own CUDA kernel (crates/core/cuda/knn.cu) -------------
+# Built unchanged by `make -C oracle _ref/libknn_ref.so` from the reference
+# tree (when it is present); the built library travels with the repository to
+# a GPU host. A second, independent checker of the oracle's flat search, and
+# a same-box floor. Never used by the product.
+
+_REF_KNN_PATH = os.path.join(_HERE, "_ref", "libknn_ref.so")
+_REF_SRC = os.environ.get("PX_REFERENCE_TREE", "/root/reference")
+_ref_lib = None
+
+
+def build_ref(force: bool = False) -> str | None:
+    """Compile _ref/libknn_ref.so from the reference tree if that tree is here."""
+    src = os.path.join(_REF_SRC, "crates", "core", "cuda", "knn.cu")
+    if not os.path.exists(src):
+        return _REF_KNN_PATH if os.path.exists(_REF_KNN_PATH) else None
+    if force or not os.path.exists(_REF_KNN_PATH) or os.path.getmtime(_REF_KNN_PATH) < os.path.getmtime(src):
+        subprocess.run(["make", "-s", "-C", _HERE, "_ref/libknn_ref.so", f"REF={_REF_SRC}"], check=True)
+    return _REF_KNN_PATH
+
+
+def ref_knn_available() -> bool:
+    return os.path.exists(_REF_KNN_PATH)
+
+
+def ref_knn_lib():
+    """ctypes handle of the reference's knn_gpu_* (signatures of gpu.rs:10-15)."""
+    global _ref_lib
+    if _ref_lib is None:
+        L = ctypes.CDLL(_REF_KNN_PATH)
+        L.knn_gpu_create.argtypes = [_f32p, ctypes.c_int, ctypes.c_int]
+        L.knn_gpu_create.restype = ctypes.c_void_p
+        L.knn_gpu_search.argtypes = [ctypes.c_void_p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                     ctypes.POINTER(ctypes.c_longlong), _f32p]
+        L.knn_gpu_search.restype = ctypes.c_int
+        L.knn_gpu_free.argtypes = [ctypes.c_void_p]
+        L.knn_gpu_free.restype = None
+        _ref_lib = L
+    return _ref_lib
+
+
+class RefKnn:
+    """The reference GPU index: knn_gpu_create / search / free (knn.cu:123-180).
+    Returns KEY-SPACE values (squared L2, or -inner product) as the kernel
+    writes them; k <= 46 (knn.cu:5)."""
+
+    def __init__(self, base: np.ndarray):
+        b = np.ascontiguousarray(base, dtype=np.float32)
+        self.dim = b.shape[1]
+        self.h = ref_knn_lib().knn_gpu_create(b.ctypes.data_as(_f32p), b.shape[0], self.dim)
+        if not self.h:
+            raise RuntimeError("knn_gpu_create failed")
+
+    def search(self, queries: np.ndarray, k: int, metric: int):
+        q = np.ascontiguousarray(queries, dtype=np.float32)
+        ids = np.empty((q.shape[0], k), dtype=np.int64)
+        keys = np.empty((q.shape[0], k), dtype=np.float32)
+        rc = ref_knn_lib().knn_gpu_search(self.h, q.ctypes.data_as(_f32p), q.shape[0], k, metric,
+                                          ids.ctypes.data_as(ctypes.POINTER(ctypes.c_longlong)),
+                                          keys.ctypes.data_as(_f32p))
+        if rc != 0:
+            raise RuntimeError(f"knn_gpu_search returned {rc}")
+        return ids, keys
+
+    def close(self):
+        if self.h:
+            ref_knn_lib().knn_gpu_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()

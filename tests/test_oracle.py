@@ -285,3 +285,42 @@ def test_check_topk_accepts_ties_and_rejects_errors():
         O.check_topk(O.L2, data, q, np.array([[0, 1, 3]], np.int64), ref_d, ref_ids, ref_d)
     with pytest.raises(AssertionError):
         O.check_topk(O.L2, data, q, np.array([[0, 0, 1]], np.int64), ref_d, ref_ids, ref_d)
+
+
+# ---- pinned by the reference's own code -------------------------------------
+
+def test_oracle_matches_reference_kernel_fixtures():
+    """The oracle's FlatIndex::search_batch against outputs of the reference's
+    CUDA kernel (crates/core/cuda/knn.cu, compiled unchanged and run on a
+    B200 by tests/golden/make_knn_ref_golden.py). Integer-valued data: keys
+    bit for bit, ids except at exact ties. Unit-norm data: the kernel sums in
+    a different order, so keys within 1e-5 relative and ids except where
+    neighbouring keys are that close."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location(
+        "make_knn_ref_golden", os.path.join(os.path.dirname(__file__), "golden", "make_knn_ref_golden.py"))
+    gen = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(gen)
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "knn_ref_golden.npz"))
+    checked = 0
+    for name, (_, n, dim, nq, seed, metrics) in gen.CASES.items():
+        base, queries = gen.case_data(name)
+        for metric in metrics:
+            for k in gen.KS:
+                ref_ids = g[f"{name}_m{metric}_k{k}_ids"]
+                ref_keys = g[f"{name}_m{metric}_k{k}_keys"]
+                ids, _ = O.flat_search_batch(base, metric, queries, k)
+                keys = np.stack([O.flat_keys(base, metric, queries[q], ids[q]) for q in range(nq)])
+                if name == "sift":
+                    assert np.array_equal(keys.view(np.uint32), ref_keys.view(np.uint32)), (name, metric, k)
+                    tol = np.zeros_like(keys)
+                else:
+                    tol = 1e-5 * np.maximum(np.abs(ref_keys), 1e-3)
+                    assert np.all(np.abs(keys - ref_keys) <= tol), (name, metric, k)
+                for q in range(nq):
+                    for j in np.nonzero(ids[q] != ref_ids[q])[0]:
+                        near = np.abs(keys[q] - keys[q, j]) <= 2 * tol[q, j]
+                        assert near.sum() > 1 or abs(keys[q, j] - keys[q, -1]) <= 2 * tol[q, j], (name, q, j)
+                checked += 1
+    assert checked == 6
