@@ -145,6 +145,26 @@ __device__ __forceinline__ void list_sort(uint64_t (&L)[CAP]) {
   }
 }
 
+// One top-CAP candidate list of an epilogue thread: unsorted words, the
+// largest of them (thr, PX_EMPTY while not full) and its position, and thr's
+// key as a float for the column tests.
+template <int CAP>
+struct TopList {
+  uint64_t L[CAP];
+  uint64_t thr;
+  float thr_key;
+  int maxpos;
+
+  // start_key: +inf (accept everything), or -inf for a padding query row.
+  __device__ __forceinline__ void reset(float start_key) {
+#pragma unroll
+    for (int j = 0; j < CAP; ++j) L[j] = PX_EMPTY;
+    thr = PX_EMPTY;
+    thr_key = start_key;
+    maxpos = 0;
+  }
+};
+
 // Approximate keys of 32 accumulator columns (base rows rbase ..): -q.x, or
 // ||x||^2 - 2 q.x with the row norms (padded to whole 256-row tiles, so every
 // chunk of a tile is in bounds).
@@ -174,32 +194,32 @@ __device__ __forceinline__ uint32_t low_bits(int n) {
 // Inserts the columns of `pass` (keys in slot[0..31], rows rbase ..) that
 // beat the running threshold into the top-CAP list.
 template <int CAP>
-__device__ __forceinline__ void insert_passing(uint64_t (&L)[CAP], uint64_t& thr, float& thr_key, int& maxpos,
-                                               uint32_t pass, const float* slot, int64_t rbase) {
+__device__ __forceinline__ void insert_passing(TopList<CAP>& T, uint32_t pass, const float* slot, int64_t rbase) {
   while (pass) {
     const int j = __ffs(pass) - 1;
     pass &= pass - 1;
     const float kj = slot[j];
-    if (kj <= thr_key) {
+    if (kj <= T.thr_key) {
       const uint64_t cand = pack_cand(kj, static_cast<uint32_t>(rbase + j));
-      if (cand < thr) {
-        list_insert<CAP>(L, thr, maxpos, cand);
-        thr_key = thr == PX_EMPTY ? __int_as_float(0x7f800000) : cand_key(thr);
+      if (cand < T.thr) {
+        list_insert<CAP>(T.L, T.thr, T.maxpos, cand);
+        T.thr_key = T.thr == PX_EMPTY ? __int_as_float(0x7f800000) : cand_key(T.thr);
       }
     }
   }
 }
 
 // Drains NCOL accumulator columns (base rows row0 ..) of this thread's TMEM
-// lane into its top-CAP list, 64 columns per step: two TMEM loads in flight
-// and one wait, approximate keys, two independent three-input min trees that
-// reject the 64 columns in the common case, and the exact per-column test and
-// insertion otherwise. taddr: the lane's TMEM address of column 0; slot: 32
-// floats of this thread in shared memory, touched only on the rare path.
+// lane, 64 columns per step: two TMEM loads in flight and one wait,
+// approximate keys, two independent three-input min trees that reject the 64
+// columns in the common case, and the exact per-column test and insertion
+// otherwise. The first 32 columns of every step go to list A, the second 32
+// to list B (A and B may be the same list). taddr: the lane's TMEM address of
+// column 0; slot: 32 floats of this thread in shared memory, touched only on
+// the rare path.
 template <int CAP, bool L2, int NCOL>
-__device__ __forceinline__ void drain_columns(uint64_t (&L)[CAP], uint64_t& thr, float& thr_key, int& maxpos,
-                                              uint32_t taddr, int64_t row0, int valid_cols,
-                                              const GemmTopkArgs& p, float* slot) {
+__device__ __forceinline__ void drain_columns(TopList<CAP>& A, TopList<CAP>& B, uint32_t taddr, int64_t row0,
+                                              int valid_cols, const GemmTopkArgs& p, float* slot) {
   static_assert(NCOL % 64 == 0, "columns are drained 64 at a time");
 #pragma unroll 1
   for (int c = 0; c < NCOL / 64; ++c) {
@@ -218,27 +238,27 @@ __device__ __forceinline__ void drain_columns(uint64_t (&L)[CAP], uint64_t& thr,
       // the common case needs no negated keys at all.
       m0 = -max32u(v0);
       m1 = -max32u(v1);
-      if (whole && !(fminf(m0, m1) <= thr_key)) continue;
+      if (whole && !(m0 <= A.thr_key) && !(m1 <= B.thr_key)) continue;
     }
     float k0[32], k1[32];
     chunk_keys<L2>(v0, p, rbase, k0);
     chunk_keys<L2>(v1, p, rbase + 32, k1);
-    // Common case: nothing in the 64 columns beats the threshold. Partial or
-    // filtered steps take the exact per-column test; otherwise only a half
-    // whose minimum can pass does.
+    // Common case: nothing in the 64 columns beats its list's threshold.
+    // Partial or filtered steps take the exact per-column test; otherwise
+    // only a half whose minimum can pass does.
     if (L2) {
       m0 = min32(k0);
       m1 = min32(k1);
-      if (whole && !(fminf(m0, m1) <= thr_key)) continue;
+      if (whole && !(m0 <= A.thr_key) && !(m1 <= B.thr_key)) continue;
     }
     uint32_t pass0 = 0, pass1 = 0;
-    if (!whole || m0 <= thr_key) {
+    if (!whole || m0 <= A.thr_key) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) pass0 |= (k0[j] <= thr_key ? 1u : 0u) << j;
+      for (int j = 0; j < 32; ++j) pass0 |= (k0[j] <= A.thr_key ? 1u : 0u) << j;
     }
-    if (!whole || m1 <= thr_key) {
+    if (!whole || m1 <= B.thr_key) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) pass1 |= (k1[j] <= thr_key ? 1u : 0u) << j;
+      for (int j = 0; j < 32; ++j) pass1 |= (k1[j] <= B.thr_key ? 1u : 0u) << j;
     }
     pass0 &= low_bits(nvalid);
     pass1 &= low_bits(nvalid - 32);
@@ -251,12 +271,12 @@ __device__ __forceinline__ void drain_columns(uint64_t (&L)[CAP], uint64_t& thr,
     if (pass0) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) slot[j] = k0[j];
-      insert_passing<CAP>(L, thr, thr_key, maxpos, pass0, slot, rbase);
+      insert_passing<CAP>(A, pass0, slot, rbase);
     }
     if (pass1) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) slot[j] = k1[j];
-      insert_passing<CAP>(L, thr, thr_key, maxpos, pass1, slot, rbase + 32);
+      insert_passing<CAP>(B, pass1, slot, rbase + 32);
     }
   }
 }
@@ -457,16 +477,12 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       const int split = item / p.T;
       const int t0 = split * p.tiles_per_split;
       const int t1 = min(p.nb, t0 + p.tiles_per_split);
-      uint64_t L[CAP];
-#pragma unroll
-      for (int j = 0; j < CAP; ++j) L[j] = PX_EMPTY;
-      uint64_t thr = PX_EMPTY;
       const int64_t qidx = static_cast<int64_t>(qp * QT + wg) * BM + row_in_tile;
       // +inf: accept everything at first. A padding query row (past nq) has
       // all-zero products, hence equal keys that would all pass and take
       // the rare insertion path on every step: -inf lets nothing in.
-      float thr_key = __int_as_float(qidx < p.nq ? 0x7f800000 : 0xff800000);
-      int maxpos = 0;
+      TopList<CAP> T;
+      T.reset(__int_as_float(qidx < p.nq ? 0x7f800000 : 0xff800000));
       for (int t = t0; t < t1; ++t) {
         // Warp-uniform decision: the tcgen05.ld below is .sync.aligned.
         const bool got = __all_sync(0xffffffffu, tc::mbar_wait(tfull_bar(acc), acc_phase, s_abort));
@@ -479,7 +495,7 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         // Columns of this tile that are real rows (the last tile may be short).
         const int valid_cols = p.n - row0 < BN ? static_cast<int>(p.n - row0) : BN;
         const uint32_t col0 = static_cast<uint32_t>((acc * QT + wg) * BN);
-        drain_columns<CAP, L2, BN>(L, thr, thr_key, maxpos, lane_addr + col0, row0, valid_cols, p, slot);
+        drain_columns<CAP, L2, BN>(T, T, lane_addr + col0, row0, valid_cols, p, slot);
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(tempty_bar(acc));
@@ -489,11 +505,11 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
       }
       if (!ok) break;
-      list_sort<CAP>(L);
+      list_sort<CAP>(T.L);
       if (qidx < p.nq) {
         uint64_t* out = p.partial + (qidx * p.S + split) * CAP;
 #pragma unroll
-        for (int j = 0; j < CAP; ++j) out[j] = L[j];
+        for (int j = 0; j < CAP; ++j) out[j] = T.L[j];
       }
     }
   }
@@ -524,8 +540,9 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 //   tfull[a]  each CTA; accumulator a holds a finished tile
 //   tempty[a] even CTA; 16 arrivals, the 8 epilogue warps of each CTA
 //   done      each CTA; every MMA has completed
-// Each CTA's two epilogue warpgroups drain 128 columns each of every tile, so
-// every (query, split) has two lists. The epilogue's rare insertion path
+// Each CTA's two epilogue warpgroups drain 128 columns each of every tile, and
+// each thread keeps two lists over alternate 32-column blocks, so every
+// (query, split) has four lists. The epilogue's rare insertion path
 // indexes its keys through a 33-float shared-memory slot per thread (local
 // memory spilled to DRAM on config 4's frequent refills). A seventh stage,
 // or prefetching base slices into L2 ahead of the ring, measured slower.
@@ -713,15 +730,15 @@ gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       const int split = item / p.T;
       const int t0 = split * p.tiles_per_split;
       const int t1 = min(p.nb, t0 + p.tiles_per_split);
-      uint64_t L[CAP];
-#pragma unroll
-      for (int j = 0; j < CAP; ++j) L[j] = PX_EMPTY;
-      uint64_t thr = PX_EMPTY;
       const int64_t qidx = static_cast<int64_t>(qg) * (2 * PM) + static_cast<int64_t>(rank) * PM + row_in_tile;
       // +inf: accept everything at first; -inf for a padding query row (see
-      // gemm_topk_kernel).
-      float thr_key = __int_as_float(qidx < p.nq ? 0x7f800000 : 0xff800000);
-      int maxpos = 0;
+      // gemm_topk_kernel). Two lists, over alternate 32-column blocks: the
+      // same number of insertions as one list of twice the size, each at
+      // half the cost.
+      const float start_key = __int_as_float(qidx < p.nq ? 0x7f800000 : 0xff800000);
+      TopList<CAP> TA, TB;
+      TA.reset(start_key);
+      TB.reset(start_key);
       for (int t = t0; t < t1; ++t) {
         const bool got = __all_sync(0xffffffffu, tc::mbar_wait(tfull_bar(acc), acc_phase, s_abort));
         if (!got) {
@@ -740,7 +757,7 @@ gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         const int64_t rem = p.n - row0;
         const int valid_cols = rem < PH ? (rem < 0 ? 0 : static_cast<int>(rem)) : PH;
         const uint32_t col0 = static_cast<uint32_t>(acc * 2 * PH + half * PH);
-        drain_columns<CAP, L2, PH>(L, thr, thr_key, maxpos, lane_addr + col0, row0, valid_cols, p, slot);
+        drain_columns<CAP, L2, PH>(TA, TB, lane_addr + col0, row0, valid_cols, p, slot);
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive_cluster(tc::mapa_shared(tempty_bar(acc), 0));
@@ -750,11 +767,14 @@ gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         }
       }
       if (!ok) break;
-      list_sort<CAP>(L);
+      list_sort<CAP>(TA.L);
+      list_sort<CAP>(TB.L);
       if (qidx < p.nq) {
-        uint64_t* out = p.partial + ((qidx * p.S + split) * 2 + half) * CAP;
+        uint64_t* out = p.partial + ((qidx * p.S + split) * 2 + half) * 2 * CAP;
 #pragma unroll
-        for (int j = 0; j < CAP; ++j) out[j] = L[j];
+        for (int j = 0; j < CAP; ++j) out[j] = TA.L[j];
+#pragma unroll
+        for (int j = 0; j < CAP; ++j) out[CAP + j] = TB.L[j];
       }
     }
   }
@@ -841,12 +861,14 @@ cudaError_t encode_bf16_map(CUtensorMap* map, const void* plane, int64_t rows, i
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-// Candidates kept per (query, split, column half) by the pair kernel. A list
-// over ~10^5 rows refills ~CAP * ln(rows / CAP) times at a cost linear in CAP,
-// while the merge needs only the best few per query from each of ~74 lists:
-// 16 keeps every k <= 16 certifiable even when one list holds all the
-// neighbours, at a quarter of the insertion work of 32; larger k keep 32.
-int gemm_pair_cap(int k) { return k <= 16 ? 16 : 32; }
+// Candidates per list of the pair kernel; every (query, split, column half)
+// has two lists, over alternate 32-column blocks. A list over R rows refills
+// ~CAP * (1 + ln(R / CAP)) times at a cost linear in CAP, so two lists of CAP
+// refill as often as one of 2 * CAP at half the cost per refill, while the
+// merge needs only the best few per query from each of ~300 lists: 2 x 8
+// keeps every k <= 16 certifiable unless 9 of a query's neighbours share one
+// list (the certificate then sends the query on), larger k keep 2 x 16.
+int gemm_pair_cap(int k) { return k <= 16 ? 8 : 16; }
 
 // Candidates rescored per query after a bf16 pass. The certificate compares
 // the k-th exact key with the largest approximate key among them, so more
@@ -870,7 +892,7 @@ int gemm_pair_clusters(int device) {
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   int clusters = 0;
-  auto kern = gemm_topk_pair_kernel<false, 16>;
+  auto kern = gemm_topk_pair_kernel<false, 8>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pairk::SMEM)) ==
       cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
@@ -915,9 +937,9 @@ cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const void* q_plane, int64_t
     e = encode_bf16_map(&maps[0], q_plane, q_rows, a.ldb, pairk::PM);
     if (e == cudaSuccess) e = encode_bf16_map(&maps[1], x_plane, a.n, a.ldb, pairk::PH);
     if (e != cudaSuccess) return e;
-    if (gemm_pair_cap(a.k) == 16)
-      return a.l2 ? launch_pair<true, 16>(a, maps, grid, stream) : launch_pair<false, 16>(a, maps, grid, stream);
-    return a.l2 ? launch_pair<true, 32>(a, maps, grid, stream) : launch_pair<false, 32>(a, maps, grid, stream);
+    if (gemm_pair_cap(a.k) == 8)
+      return a.l2 ? launch_pair<true, 8>(a, maps, grid, stream) : launch_pair<false, 8>(a, maps, grid, stream);
+    return a.l2 ? launch_pair<true, 16>(a, maps, grid, stream) : launch_pair<false, 16>(a, maps, grid, stream);
   } else {
     const bool il = kind == kPass3xTf32;
     e = encode_split_map(&maps[0], static_cast<const float*>(q_plane), q_rows, a.ld, BM, il);

@@ -152,7 +152,7 @@ int gemm_cands_for(int k);  // candidates per query after the split merge (<= 25
 int gemm_qt_for(int k);   // query tiles of 128 per CTA (2 for k <= 16, else 1)
 int gemm_bn_for(int k);   // base rows per tile (256 / qt)
 // CTA pairs of the bf16 pass's kernel that fit on `device` at once (each
-// pair takes 256 queries x 256 base rows per tile, two lists per split).
+// pair takes 256 queries x 256 base rows per tile, four lists per split).
 int gemm_pair_clusters(int device);
 int gemm_pair_cap(int k);    // candidates per list of the pair kernel (the bf16 pass)
 int gemm_pair_cands(int k);  // candidates per query after a bf16 pass (0: k too large for it)
@@ -160,7 +160,8 @@ int gemm_pair_cands(int k);  // candidates per query after a bf16 pass (0: k too
 // passes, the bf16 planes (stride ldb) for kPassBf16, which serves
 // gemm_pair_cands(k) > 0 only and runs on CTA pairs: grid is then an even
 // number of CTAs, T counts groups of 256 queries, nb tiles of 256 rows, and
-// partial holds two lists per split ([nq][S][2][cap]). kPassTf32 reads only
+// partial holds four lists per split ([nq][S][2 column halves][2][cap]).
+// kPassTf32 reads only
 // the hi halves.
 cudaError_t launch_gemm_topk(const GemmTopkArgs& a, const void* q_plane, int64_t q_rows,
                              const void* x_plane, PassKind kind, int grid, cudaStream_t stream);

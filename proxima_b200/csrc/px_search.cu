@@ -72,7 +72,7 @@ static void plan_gemm(const FlatShard& sh, int64_t nq, int k, PassKind kind, Sea
   S = (nb + tps - 1) / tps;
   plan.T = static_cast<int>(T);
   plan.S = static_cast<int>(S);
-  plan.lists = static_cast<int>(pair ? 2 * S : S);
+  plan.lists = static_cast<int>(pair ? 4 * S : S);
   plan.nb = static_cast<int>(nb);
   plan.tiles_per_split = static_cast<int>(tps);
   plan.n_items = static_cast<int>(T * S);
