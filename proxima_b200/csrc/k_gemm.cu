@@ -108,20 +108,28 @@ __device__ __forceinline__ float min32(const float (&k)[32]) {
   return fminf(min3f(b0, b1, b2), b3);
 }
 
+// Replaces the list's largest entry by cand and finds the new largest key.
+// The scan compares keys only (the words' high halves): among entries with
+// the largest key it keeps the first, and the threshold becomes the largest
+// word with that key, so a later candidate with an equal key may replace an
+// equal one. Either way every row the list drops has a key >= the list's
+// largest key, which is all the certificate relies on; words stay distinct.
 template <int CAP>
 __device__ __forceinline__ void list_insert(uint64_t (&L)[CAP], uint64_t& thr, int& maxpos,
                                             uint64_t cand) {
 #pragma unroll
   for (int j = 0; j < CAP; ++j) L[j] = (j == maxpos) ? cand : L[j];
-  thr = L[0];
+  uint32_t hi = static_cast<uint32_t>(L[0] >> 32);
   maxpos = 0;
 #pragma unroll
   for (int j = 1; j < CAP; ++j) {
-    if (L[j] > thr) {
-      thr = L[j];
+    const uint32_t h = static_cast<uint32_t>(L[j] >> 32);
+    if (h > hi) {
+      hi = h;
       maxpos = j;
     }
   }
+  thr = (static_cast<uint64_t>(hi) << 32) | 0xFFFFFFFFull;
 }
 
 template <int CAP>
