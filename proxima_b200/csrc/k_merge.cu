@@ -13,9 +13,16 @@ namespace {
 
 constexpr int kMergeWarps = 4;
 
+// Per-warp shared memory for a staged copy of one query's lists (the
+// tournament's refills then read shared memory, not a dependent global load
+// per step); larger lists merge straight from global memory.
+constexpr size_t kMergeStageBytes = 40 * 1024;
+
 // One warp per query: a k-step tournament over `nlists` sorted lists. Each
 // lane owns lists lane, lane+32, ...; it caches the smallest of its heads and
-// rescans only after its own list advanced.
+// rescans only after its own list advanced. STAGED: the query's lists are
+// first copied to shared memory with coalesced loads.
+template <bool STAGED>
 __global__ void __launch_bounds__(kMergeWarps * 32)
 merge_lists_kernel(const uint64_t* __restrict__ lists, int64_t nq, int nlists, int list_len,
                    int k, uint64_t* __restrict__ out) {
@@ -28,6 +35,17 @@ merge_lists_kernel(const uint64_t* __restrict__ lists, int64_t nq, int nlists, i
   const int64_t q = static_cast<int64_t>(blockIdx.x) * kMergeWarps + warp;
   if (q >= nq) return;
   const uint64_t* ql = lists + q * static_cast<int64_t>(nlists) * list_len;
+  if constexpr (STAGED) {
+    // After heads ([warps][nlists] u64) and pos ([warps][nlists] int),
+    // rounded up to 16 bytes.
+    const size_t fixed = (static_cast<size_t>(kMergeWarps) * nlists * (sizeof(uint64_t) + sizeof(int)) + 15) & ~size_t(15);
+    uint64_t* stage = reinterpret_cast<uint64_t*>(smem_raw + fixed) +
+                      static_cast<size_t>(warp) * nlists * list_len;
+    const int total = nlists * list_len;
+    for (int i = lane; i < total; i += 32) stage[i] = __ldg(ql + i);
+    __syncwarp();
+    ql = stage;
+  }
 
   uint64_t best = PX_EMPTY;
   int best_list = -1;
@@ -144,13 +162,16 @@ __global__ void merge_shards_kernel(const char* __restrict__ keys, int64_t key_s
 cudaError_t launch_merge_lists(const uint64_t* lists, int64_t nq, int nlists, int list_len, int k,
                                uint64_t* out, cudaStream_t stream) {
   if (nq == 0 || k == 0) return cudaSuccess;
-  const size_t smem = static_cast<size_t>(kMergeWarps) * nlists * (sizeof(uint64_t) + sizeof(int));
-  cudaError_t e = cudaFuncSetAttribute(merge_lists_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  const size_t fixed =
+      (static_cast<size_t>(kMergeWarps) * nlists * (sizeof(uint64_t) + sizeof(int)) + 15) & ~size_t(15);
+  const size_t stage = sizeof(uint64_t) * static_cast<size_t>(nlists) * list_len;
+  const bool staged = stage <= kMergeStageBytes;
+  const size_t smem = fixed + (staged ? kMergeWarps * stage : 0);
+  auto kern = staged ? merge_lists_kernel<true> : merge_lists_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const int64_t blocks = (nq + kMergeWarps - 1) / kMergeWarps;
-  merge_lists_kernel<<<static_cast<unsigned>(blocks), kMergeWarps * 32, smem, stream>>>(
-      lists, nq, nlists, list_len, k, out);
+  kern<<<static_cast<unsigned>(blocks), kMergeWarps * 32, smem, stream>>>(lists, nq, nlists, list_len, k, out);
   return cudaGetLastError();
 }
 

@@ -175,8 +175,18 @@ rescore_kernel(const RescoreArgs a) {
     const float* x = a.base + static_cast<int64_t>(row) * a.ld;
     float acc = 0.f;
     if (valid) {
-#pragma unroll 4
-      for (int cc = 0; cc < chunks; ++cc) acc = __fadd_rn(acc, lane_term<L2>(s_q[cc * 8 + l], x[cc * 8 + l]));
+      // The row is a random gather: fetch kBatch of this lane's elements
+      // before adding them in order, so kBatch loads are in flight per
+      // thread instead of the few an unrolled add chain exposes.
+      constexpr int kBatch = 16;
+      for (int c0 = 0; c0 < chunks; c0 += kBatch) {
+        float xv[kBatch];
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) xv[b] = c0 + b < chunks ? __ldg(x + (c0 + b) * 8 + l) : 0.f;
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b)
+          if (c0 + b < chunks) acc = __fadd_rn(acc, lane_term<L2>(s_q[(c0 + b) * 8 + l], xv[b]));
+      }
     }
     float sum = __shfl_sync(0xffffffffu, acc, g0);
 #pragma unroll
