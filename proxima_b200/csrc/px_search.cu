@@ -28,7 +28,6 @@ namespace {
 
 constexpr int kGemmMinQueries = 16;
 constexpr int kGemmMinRows = 4096;
-constexpr int64_t kMinSplitTiles = 32;  // base tiles per split below which lists stay loose
 
 int64_t gcd64(int64_t a, int64_t b) {
   while (b) {
@@ -59,15 +58,14 @@ static void plan_gemm(const FlatShard& sh, int64_t nq, int k, PassKind kind, Sea
   while (S * 2 <= 1024 && S * T < 2 * workers && S * 2 <= nb) S *= 2;
   S = std::min<int64_t>(S, nb);
   S = std::max<int64_t>(S, 1);
-  // Short splits: each (query, split) list starts with a loose threshold,
-  // and until it tightens most column steps take the epilogue's insertion
-  // path, so many short lists cost more than their MMAs. When the splits
-  // above would be shorter than kMinSplitTiles, one wave of longer splits
-  // (if it keeps nine tenths of the workers busy) does the same MMA work
-  // with fewer lists: config 1 goes from 36 splits of 11 tiles to 18 of 22.
+  // Fewer, longer splits: each (query, split) list starts with a loose
+  // threshold and refills about CAP * (1 + ln(rows / CAP)) times, so a list
+  // twice as long costs far less than two lists. When one wave of longer
+  // splits keeps nine tenths of the workers busy it does the same MMA work
+  // with fewer lists: config 1 goes from 36 splits of 11 tiles to 18 of 22,
+  // config 2 (4 query groups) from 37 splits to 18.
   const int64_t one_wave = workers / T;
-  if ((nb + S - 1) / S < kMinSplitTiles && one_wave >= 1 && one_wave < S && T * one_wave * 10 >= workers * 9)
-    S = std::min<int64_t>(one_wave, nb);
+  if (one_wave >= 1 && one_wave < S && T * one_wave * 10 >= workers * 9) S = std::min<int64_t>(one_wave, nb);
   const int64_t tps = (nb + S - 1) / S;
   S = (nb + tps - 1) / tps;
   plan.T = static_cast<int>(T);
