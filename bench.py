@@ -57,6 +57,8 @@ CONFIGS = {
     "prof": ("ip", 262_144, 768, 18_944, 10, "unit"),
     # profiling case for ncu: config 5's distribution on 2M rows (2.8 GB on the device)
     "prof5": ("l2", 2_000_000, 96, 10_000, 10, "mixture"),
+    # the same rows with 74 query groups over 2 splits: lists as long as config 5's
+    "prof5l": ("l2", 2_000_000, 96, 18_944, 10, "mixture"),
     # PQ ADC scan (config 3): m=16 x 256 centroids trained on a 100k sample
     "c3": ("pq-l2", 1_000_000, 128, 1_000, 10, "sift"),
 }
@@ -74,6 +76,8 @@ WORKLOAD_TEXT = {
              "(2.8 GB on the device; 131k rows per split, as config 4 has 270k)"),
     "prof5": ("profiling case: exact L2 kNN, config 5's Gaussian mixture on 2,000,000x96 rows, 10,000 "
               "queries, k=10 (2.8 GB on the device)"),
+    "prof5l": ("profiling case: exact L2 kNN, config 5's Gaussian mixture on 2,000,000x96 rows, 18,944 "
+               "queries (74 query groups over 2 splits, 250k rows per list), k=10 (2.9 GB on the device)"),
     "c3": "PQ ADC scan, L2, m=16 x 256 centroids (k-means on a 100,000-row sample), 1,000,000 codes, "
           "1,000 queries, k=10 (config 3)",
 }
