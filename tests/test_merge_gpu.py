@@ -111,3 +111,50 @@ def test_merge_shards_matches_single_index(px, oracle_lib, G, metric, n, k):
     torch.cuda.synchronize()
     assert np.array_equal(out_i.cpu().numpy(), got_i)
     assert np.array_equal(out_d.cpu().numpy().view(np.uint32), got_d.view(np.uint32))
+
+
+@pytest.mark.parametrize("metric", [O.L2, O.IP])
+def test_sharded_index_record_path_on_one_gpu(px, oracle_lib, monkeypatch, metric):
+    """ShardedFlatIndex.search_device for two ranks, both on one GPU, with the
+    all-gather replaced by a local copy of the two ranks' records (NCCL needs
+    one GPU per rank). Exercises what every rank does around the collective:
+    the key-space search written into its record, the record layout, and the
+    record merge; the answer must equal the oracle's on the whole base."""
+    import torch
+
+    import proxima_b200.distributed as D
+    from proxima_b200.distributed import ShardedFlatIndex
+
+    assert px.device_count() > 0, "GPU tests need a CUDA device"
+    rng = np.random.default_rng(4)
+    n, dim, nq, k = 9001, 64, 37, 10
+    data = np.rint(rng.standard_normal((n, dim)).astype(np.float32) * 3)
+    data[4600:4700] = data[:100]  # exact ties across the two shards
+    queries = np.rint(rng.standard_normal((nq, dim)).astype(np.float32) * 3)
+    ranks = []
+    for r in range(2):
+        idx = ShardedFlatIndex(dim, px.Metric.L2 if metric == O.L2 else px.Metric.InnerProduct, device=0)
+        idx.world, idx.rank, idx._bufs = 2, r, {}
+        lo, hi = shard_range(n, 2, r)
+        idx.set_offset(lo)
+        idx.add_local(data[lo:hi])
+        ranks.append(idx)
+    dq = torch.from_numpy(queries).cuda()
+    records = {}
+
+    def fake_all_gather(out, inp, group=None):
+        records[len(records)] = inp.clone()
+        if len(records) == 2:
+            out.copy_(torch.cat([records[0], records[1]]))
+        else:
+            out.fill_(255)  # rank 0 merges before rank 1 has searched: all ids -1, i.e. padding
+
+    monkeypatch.setattr(D.dist, "all_gather_into_tensor", fake_all_gather)
+    for path in ("tensor", "exact"):
+        records.clear()
+        for idx in ranks:
+            idx.local.set_search_path(path)
+        ranks[0].search_device(dq, k)  # rank 0's record; its merge waits for rank 1's
+        ids, d = ranks[1].search_device(dq, k)
+        torch.cuda.synchronize()
+        _parity.check_flat(data, metric, queries, ids.cpu().numpy(), d.cpu().numpy(), k)
