@@ -55,6 +55,8 @@ CONFIGS = {
     "c5s": ("l2", 10_000_000, 96, 10_000, 10, "mixture"),
     # profiling case for ncu: config 4's distribution and rows per split on 1/38 of the rows
     "prof": ("ip", 262_144, 768, 18_944, 10, "unit"),
+    # config 4's 40 query groups on the profiling case's rows (short splits)
+    "prof40": ("ip", 262_144, 768, 10_000, 10, "unit"),
     # profiling case for ncu: config 5's distribution on 2M rows (2.8 GB on the device)
     "prof5": ("l2", 2_000_000, 96, 10_000, 10, "mixture"),
     # the same rows with 74 query groups over 2 splits: lists as long as config 5's
@@ -74,6 +76,8 @@ WORKLOAD_TEXT = {
             "mixture, 10,000 queries, k=10"),
     "prof": ("profiling case: exact IP kNN, base 262,144x768 unit-norm N(0,1), 18,944 queries, k=10 "
              "(2.8 GB on the device; 131k rows per split, as config 4 has 270k)"),
+    "prof40": ("profiling case: exact IP kNN, base 262,144x768 unit-norm N(0,1), 10,000 queries (config 4's "
+               "40 query groups, 37 splits of 28 tiles), k=10 (2.8 GB on the device)"),
     "prof5": ("profiling case: exact L2 kNN, config 5's Gaussian mixture on 2,000,000x96 rows, 10,000 "
               "queries, k=10 (2.8 GB on the device)"),
     "prof5l": ("profiling case: exact L2 kNN, config 5's Gaussian mixture on 2,000,000x96 rows, 18,944 "
