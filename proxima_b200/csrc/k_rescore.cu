@@ -178,7 +178,7 @@ rescore_kernel(const RescoreArgs a) {
       // The row is a random gather: fetch kBatch of this lane's elements
       // before adding them in order, so kBatch loads are in flight per
       // thread instead of the few an unrolled add chain exposes.
-      constexpr int kBatch = 16;
+      constexpr int kBatch = 48;
       for (int c0 = 0; c0 < chunks; c0 += kBatch) {
         float xv[kBatch];
 #pragma unroll
