@@ -17,6 +17,27 @@ constexpr int kMergeWarps = 4;
 // tournament's refills then read shared memory, not a dependent global load
 // per step); larger lists merge straight from global memory.
 constexpr size_t kMergeStageBytes = 40 * 1024;
+// From this many output words on, the merge selects by value search
+// (merge_select_kernel) rather than popping one word per tournament step.
+constexpr int kMergeSelectMinK = 128;
+
+// Copies n words to shared memory, eight loads in flight per lane (a plain
+// load-store loop would wait out a global-memory latency per word).
+__device__ __forceinline__ void stage_words(uint64_t* dst, const uint64_t* __restrict__ src, int n, int lane) {
+  for (int i0 = 0; i0 < n; i0 += 32 * 8) {
+    uint64_t v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * 32 + lane;
+      v[u] = i < n ? __ldg(src + i) : 0ull;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * 32 + lane;
+      if (i < n) dst[i] = v[u];
+    }
+  }
+}
 
 // One warp per query: a k-step tournament over `nlists` sorted lists. Each
 // lane owns lists lane, lane+32, ...; it caches the smallest of its heads and
@@ -41,8 +62,7 @@ merge_lists_kernel(const uint64_t* __restrict__ lists, int64_t nq, int nlists, i
     const size_t fixed = (static_cast<size_t>(kMergeWarps) * nlists * (sizeof(uint64_t) + sizeof(int)) + 15) & ~size_t(15);
     uint64_t* stage = reinterpret_cast<uint64_t*>(smem_raw + fixed) +
                       static_cast<size_t>(warp) * nlists * list_len;
-    const int total = nlists * list_len;
-    for (int i = lane; i < total; i += 32) stage[i] = __ldg(ql + i);
+    stage_words(stage, ql, nlists * list_len, lane);
     __syncwarp();
     ql = stage;
   }
@@ -92,6 +112,103 @@ merge_lists_kernel(const uint64_t* __restrict__ lists, int64_t nq, int nlists, i
     }
     __syncwarp();
   }
+}
+
+// Number of words <= v in a sorted list of len words (an upper bound).
+__device__ __forceinline__ int count_le_sorted(const uint64_t* L, int len, uint64_t v) {
+  int lo = 0, hi = len;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (L[mid] <= v) lo = mid + 1;
+    else hi = mid;
+  }
+  return lo;
+}
+
+// One warp per query, for large k: the k smallest words of `nlists` sorted
+// lists, without a k-step tournament. The query's lists are staged in shared
+// memory; the k-th smallest word T is found bit by bit, counting the words
+// <= a trial value with a binary search in each list (32 steps over the key
+// half; 32 more over the row half only when the boundary key repeats, since
+// all words of a query are distinct: distinct rows). The words <= T are then
+// gathered and sorted with a warp bitonic sort.
+__global__ void __launch_bounds__(kMergeWarps * 32)
+merge_select_kernel(const uint64_t* __restrict__ lists, int64_t nq, int nlists, int list_len, int k, int kp,
+                    uint64_t* __restrict__ out) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = nlists * list_len;
+  uint64_t* stage = reinterpret_cast<uint64_t*>(smem_raw) + static_cast<size_t>(warp) * (total + kp);
+  uint64_t* sel = stage + total;
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * kMergeWarps + warp;
+  if (q >= nq) return;
+  const uint64_t* ql = lists + q * static_cast<int64_t>(total);
+  stage_words(stage, ql, total, lane);
+  __syncwarp();
+  auto count_le = [&](uint64_t v) {
+    int c = 0;
+    for (int l = lane; l < nlists; l += 32) c += count_le_sorted(stage + l * list_len, list_len, v);
+    return __reduce_add_sync(0xffffffffu, c);
+  };
+  // Real (non-empty) words: PX_EMPTY is the largest word.
+  const int real = count_le(PX_EMPTY - 1);
+  const int kk = real < k ? real : k;
+  uint64_t t = 0;  // the threshold: exactly kk words are <= t
+  if (kk > 0) {
+    uint32_t hi = 0;  // smallest key half with at least kk words at or below it
+    for (int b = 31; b >= 0; --b) {
+      const uint32_t trial = hi | ((1u << b) - 1u);
+      if (count_le((static_cast<uint64_t>(trial) << 32) | 0xFFFFFFFFull) < kk) hi |= 1u << b;
+    }
+    t = (static_cast<uint64_t>(hi) << 32) | 0xFFFFFFFFull;
+    if (count_le(t) != kk) {  // the boundary key repeats: resolve on the row half
+      uint32_t lo = 0;
+      for (int b = 31; b >= 0; --b) {
+        const uint32_t trial = lo | ((1u << b) - 1u);
+        if (count_le((static_cast<uint64_t>(hi) << 32) | trial) < kk) lo |= 1u << b;
+      }
+      t = (static_cast<uint64_t>(hi) << 32) | lo;
+    }
+  }
+  // Gather the kk words <= t: each lane's lists' prefixes, at offsets from an
+  // exclusive scan of the lanes' counts.
+  int mine = 0;
+  if (kk > 0)
+    for (int l = lane; l < nlists; l += 32) mine += count_le_sorted(stage + l * list_len, list_len, t);
+  int incl = mine;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += o;
+  }
+  int at = incl - mine;
+  if (kk > 0) {
+    for (int l = lane; l < nlists; l += 32) {
+      const uint64_t* L = stage + l * list_len;
+      const int c = count_le_sorted(L, list_len, t);
+      for (int i = 0; i < c && at < kp; ++i) sel[at++] = L[i];  // at most kk (<= kp) words qualify
+    }
+  }
+  __syncwarp();
+  for (int i = kk + lane; i < kp; i += 32) sel[i] = PX_EMPTY;
+  __syncwarp();
+  // Bitonic sort of kp (a power of two) words, ascending.
+  for (int size = 2; size <= kp; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int p = lane; p < kp / 2; p += 32) {
+        const int lo_i = 2 * stride * (p / stride) + (p % stride);
+        const int hi_i = lo_i + stride;
+        const bool up = (lo_i & size) == 0;
+        const uint64_t a = sel[lo_i], b = sel[hi_i];
+        if ((a > b) == up) {
+          sel[lo_i] = b;
+          sel[hi_i] = a;
+        }
+      }
+      __syncwarp();
+    }
+  }
+  for (int j = lane; j < k; j += 32) out[q * k + j] = sel[j];
 }
 
 __device__ __forceinline__ int64_t map_row(uint32_t row, const IdSegments& s) {
@@ -166,6 +283,19 @@ cudaError_t launch_merge_lists(const uint64_t* lists, int64_t nq, int nlists, in
       (static_cast<size_t>(kMergeWarps) * nlists * (sizeof(uint64_t) + sizeof(int)) + 15) & ~size_t(15);
   const size_t stage = sizeof(uint64_t) * static_cast<size_t>(nlists) * list_len;
   const bool staged = stage <= kMergeStageBytes;
+  // Large k: select by value search instead of a k-step tournament.
+  if (staged && k >= kMergeSelectMinK && k <= 1024) {
+    int kp = 1;
+    while (kp < k) kp <<= 1;
+    const size_t smem = static_cast<size_t>(kMergeWarps) * (stage + sizeof(uint64_t) * kp);
+    cudaError_t e = cudaFuncSetAttribute(merge_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    const int64_t blocks = (nq + kMergeWarps - 1) / kMergeWarps;
+    merge_select_kernel<<<static_cast<unsigned>(blocks), kMergeWarps * 32, smem, stream>>>(lists, nq, nlists,
+                                                                                          list_len, k, kp, out);
+    return cudaGetLastError();
+  }
   const size_t smem = fixed + (staged ? kMergeWarps * stage : 0);
   auto kern = staged ? merge_lists_kernel<true> : merge_lists_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
