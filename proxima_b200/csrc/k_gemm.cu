@@ -199,6 +199,16 @@ __device__ __forceinline__ uint32_t low_bits(int n) {
   return n <= 0 ? 0u : (n >= 32 ? 0xffffffffu : (1u << n) - 1u);
 }
 
+// Inserts one column (key, row) if it beats the list's threshold.
+template <int CAP>
+__device__ __forceinline__ void insert_one(TopList<CAP>& T, float key, int64_t row) {
+  const uint64_t cand = pack_cand(key, static_cast<uint32_t>(row));
+  if (cand < T.thr) {
+    list_insert<CAP>(T.L, T.thr, T.maxpos, cand);
+    T.thr_key = T.thr == PX_EMPTY ? __int_as_float(0x7f800000) : cand_key(T.thr);
+  }
+}
+
 // Inserts the columns of `pass` (keys in slot[0..31], rows rbase ..) that
 // beat the running threshold into the top-CAP list.
 template <int CAP>
@@ -274,17 +284,27 @@ __device__ __forceinline__ void drain_columns(TopList<CAP>& A, TopList<CAP>& B, 
       pass0 &= __ldg(p.mask_bits + (rbase >> 5));
       pass1 &= __ldg(p.mask_bits + (rbase >> 5) + 1);
     }
-    // Rare path: the keys of a half with a passing column go through this
+    // Rare path. In a whole block a single passing column is the block's
+    // minimum (it passes whenever anything does), whose key m is already at
+    // hand: insert it directly. Otherwise the half's keys go through this
     // thread's shared-memory slot so they can be indexed.
     if (pass0) {
+      if (whole && (pass0 & (pass0 - 1)) == 0) {
+        insert_one<CAP>(A, m0, rbase + __ffs(pass0) - 1);
+      } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) slot[j] = k0[j];
-      insert_passing<CAP>(A, pass0, slot, rbase);
+        for (int j = 0; j < 32; ++j) slot[j] = k0[j];
+        insert_passing<CAP>(A, pass0, slot, rbase);
+      }
     }
     if (pass1) {
+      if (whole && (pass1 & (pass1 - 1)) == 0) {
+        insert_one<CAP>(B, m1, rbase + 32 + __ffs(pass1) - 1);
+      } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) slot[j] = k1[j];
-      insert_passing<CAP>(B, pass1, slot, rbase + 32);
+        for (int j = 0; j < 32; ++j) slot[j] = k1[j];
+        insert_passing<CAP>(B, pass1, slot, rbase + 32);
+      }
     }
   }
 }
