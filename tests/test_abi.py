@@ -102,3 +102,30 @@ def test_python_mirror_validation_without_gpu(px):
         pq.search(np.zeros(64, np.float32), k=5)
     with pytest.raises(ValueError, match="not trained"):
         pq.search_filtered(np.zeros(64, np.float32), np.zeros(0, bool), k=5)
+
+
+def test_record_layout_and_new_entry_points_validate_without_gpu(px):
+    """The shard-record size and the argument checks of the entry points this
+    library adds beside the reference's (they fail before any device work)."""
+    lib = px._lib.load()
+    # ids (8 bytes) then keys (4 bytes) per entry, padded to 16 bytes.
+    for nq, k in ((1, 1), (37, 10), (10000, 10), (3, 7), (0, 5)):
+        rec = lib.px_shard_record_bytes(nq, k)
+        assert rec % 16 == 0 and 12 * nq * k <= rec < 12 * nq * k + 16, (nq, k, rec)
+    assert lib.px_shard_record_bytes(-1, 3) == 0
+    vp = ctypes.c_void_p
+    # Record merge: shard count, sizes and metric are checked first.
+    assert lib.px_merge_shard_records_device(0, vp(16), 0, 1, 1, 0, 1, vp(16), vp(16), None) == px._lib.PX_EINVAL
+    assert lib.px_merge_shard_records_device(0, vp(16), 9, 1, 1, 0, 1, vp(16), vp(16), None) == px._lib.PX_EINVAL
+    assert lib.px_merge_shard_records_device(0, vp(16), 2, -1, 1, 0, 1, vp(16), vp(16), None) == px._lib.PX_EINVAL
+    assert lib.px_merge_shard_records_device(0, vp(16), 2, 1, 1, 5, 1, vp(16), vp(16), None) == px._lib.PX_EINVAL
+    assert lib.px_merge_shard_records_device(0, None, 2, 1, 1, 0, 1, vp(16), vp(16), None) == px._lib.PX_EINVAL
+    assert lib.px_merge_shard_records_device(0, vp(8), 2, 1, 1, 0, 1, vp(16), vp(16), None) == px._lib.PX_EINVAL
+    assert "16-byte aligned" in px._lib.last_error()
+    # Nothing to merge is a no-op.
+    assert lib.px_merge_shard_records_device(0, None, 2, 0, 1, 0, 1, None, None, None) == 0
+    # Null handles.
+    cands, kind = ctypes.c_int32(0), ctypes.c_int32(0)
+    assert lib.px_flat_debug_candidates(None, None, 1, 10, 64, None, None, ctypes.byref(cands),
+                                        ctypes.byref(kind)) == px._lib.PX_EINVAL
+    assert lib.px_pq_search_device(None, None, 1, 10, 0, None, None, None) == px._lib.PX_EINVAL
