@@ -556,6 +556,7 @@ def run_ours(args, cfg, rank, world, local_rank):
             flops = 2.0 * nq * n_local * dim
             achieved = flops / avg_s / 1e12
             first = index.local.last_search_profile()["first_pass"]
+            sample_tiles = index.local.last_search_profile()["sample_tiles"]
             # bf16 MMAs issue at the measured bf16 rate, tf32 at half of it,
             # and the 3xTF32 sum takes three tf32 MMAs per product.
             peak = pk["bf16_tflops_sustained"] / {"bf16": 1.0, "tf32": 2.0, "3xtf32": 6.0}[first]
@@ -569,6 +570,9 @@ def run_ours(args, cfg, rank, world, local_rank):
                                    "tf32": "gemm_topk_kernel (tcgen05 kind::tf32, hi values)",
                                    "3xtf32": "gemm_topk_kernel (tcgen05 kind::tf32, 3xTF32 sum)"}[first],
                         "kernel_ms": statistics.mean(kernel_ms),
+                        # The timed span starts before the sample pass (that
+                        # many single base tiles per query group) and its merge.
+                        "sample_pass_tiles": sample_tiles,
                         "peak_basis": {"bf16": "bf16 rate = bf16_tflops_sustained",
                                        "tf32": "TF32 rate = bf16_tflops_sustained / 2",
                                        "3xtf32": "3xTF32 rate = bf16_tflops_sustained / 2 / 3"}[first]

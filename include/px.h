@@ -115,6 +115,14 @@ PX_API px_status px_flat_read_rows(const px_flat* h, int64_t start, int64_t coun
 enum { PX_PATH_AUTO = 0, PX_PATH_EXACT = 1, PX_PATH_TENSOR = 2, PX_PATH_TENSOR_3XTF32 = 3 };
 PX_API px_status px_flat_set_path(px_flat* h, int32_t mode);
 
+/* The bf16 pass's sample pass (a first pass over 32 base tiles spread over
+ * the shard, whose per-query thresholds the main pass's lists start from):
+ * AUTO runs it on shards of at least 128 tiles of 256 rows whose splits are
+ * at least 512 tiles long; ON on every shard of at least 128 tiles; OFF
+ * never. Results are identical either way. */
+enum { PX_SAMPLE_AUTO = 0, PX_SAMPLE_OFF = 1, PX_SAMPLE_ON = 2 };
+PX_API px_status px_flat_set_sample_pass(px_flat* h, int32_t mode);
+
 /* Per-search instrumentation (off by default). With profiling on, the
  * dominant kernel of each search is bracketed by CUDA events on the
  * launching stream; px_flat_last_profile waits for them and reports. */
@@ -127,6 +135,8 @@ typedef struct px_search_profile {
   int32_t refined_queries;  /* queries re-run by the three-pass tensor-core pass */
   int32_t first_pass;       /* tensor-core path: operands of the first candidate
                                pass, 0 three-pass tf32, 1 tf32, 2 bf16; else -1 */
+  int32_t sample_tiles;     /* base tiles of the bf16 pass's sample pass, which
+                               sets the lists' starting thresholds (0: none) */
 } px_search_profile;
 PX_API void px_set_profiling(int32_t enable);
 PX_API px_status px_flat_last_profile(const px_flat* h, px_search_profile* out);

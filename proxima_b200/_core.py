@@ -233,6 +233,15 @@ class FlatIndex:
         changes speed."""
         _lib.check(self._lib.px_flat_set_path(self._h, self._PATHS[path]))
 
+    _SAMPLE = {"auto": 0, "off": 1, "on": 2}
+
+    def set_sample_pass(self, mode: str) -> None:
+        """The bf16 pass's sample pass: "auto" (default: shards of at least
+        128 tiles whose splits are at least 512 tiles long), "on" (every
+        shard of at least 128 tiles) or "off". Results are identical either
+        way; this only changes speed."""
+        _lib.check(self._lib.px_flat_set_sample_pass(self._h, self._SAMPLE[mode]))
+
     def last_search_profile(self) -> dict:
         """Path, kernel launches, queries the certificate sent to the
         three-pass refinement and to the exact scan, and (when profiling is
@@ -243,6 +252,7 @@ class FlatIndex:
         return {"path": ("exact", "tensor")[prof.path], "launches": prof.launches,
                 "fallback_queries": prof.fallback_queries, "refined_queries": prof.refined_queries,
                 "first_pass": {0: "3xtf32", 1: "tf32", 2: "bf16"}.get(prof.first_pass),
+                "sample_tiles": prof.sample_tiles,
                 "main_kernel_ms": prof.main_kernel_ms if prof.profiled else None}
 
 

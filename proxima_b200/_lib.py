@@ -46,7 +46,7 @@ class SearchProfile(ctypes.Structure):
     _fields_ = [("path", ctypes.c_int32), ("launches", ctypes.c_int32),
                 ("fallback_queries", ctypes.c_int32), ("profiled", ctypes.c_int32),
                 ("main_kernel_ms", ctypes.c_float), ("refined_queries", ctypes.c_int32),
-                ("first_pass", ctypes.c_int32)]
+                ("first_pass", ctypes.c_int32), ("sample_tiles", ctypes.c_int32)]
 
 
 SIGNATURES = {
@@ -68,6 +68,7 @@ SIGNATURES = {
     "px_flat_metric": (_i32, [_vp]),
     "px_flat_set_id_offset": (_i32, [_vp, _i64]),
     "px_flat_set_path": (_i32, [_vp, _i32]),
+    "px_flat_set_sample_pass": (_i32, [_vp, _i32]),
     "px_set_profiling": (None, [_i32]),
     "px_flat_last_profile": (_i32, [_vp, _vp]),
     "px_launch_count": (_i64, []),

@@ -154,24 +154,44 @@ __device__ __forceinline__ void list_sort(uint64_t (&L)[CAP]) {
 }
 
 // One top-CAP candidate list of an epilogue thread: unsorted words, the
-// largest of them (thr, PX_EMPTY while not full) and its position, and thr's
-// key as a float for the column tests.
+// largest of them (thr, PX_EMPTY while not full) and its position, thr's key
+// as a float for the column tests, and the key the list admits while it is
+// not full (open_key).
 template <int CAP>
 struct TopList {
   uint64_t L[CAP];
   uint64_t thr;
   float thr_key;
+  float open_key;
   int maxpos;
 
-  // start_key: +inf (accept everything), or -inf for a padding query row.
+  // start_key: +inf (accept everything), a sample pass's k-th key, or -inf
+  // for a padding query row.
   __device__ __forceinline__ void reset(float start_key) {
 #pragma unroll
     for (int j = 0; j < CAP; ++j) L[j] = PX_EMPTY;
     thr = PX_EMPTY;
     thr_key = start_key;
+    open_key = start_key;
     maxpos = 0;
   }
 };
+
+// The key a query's lists start from. Without a seed every list is open
+// (+inf). With one, seed[qidx][seed_k - 1] is the seed_k-th best word a
+// sample pass found (seed_k >= k): seed_k real rows have keys <= its key, so
+// no row above it can be in the top k, and the lists admit only keys <= it
+// (fewer than seed_k sample candidates: open). A padding query row (past nq) has all-zero products,
+// hence equal keys that would all pass and take the rare insertion path on
+// every step: -inf lets nothing in.
+__device__ __forceinline__ float list_start_key(const GemmTopkArgs& p, int64_t qidx) {
+  if (qidx >= p.nq) return __int_as_float(0xff800000);
+  if (p.seed != nullptr) {
+    const uint64_t w = p.seed[qidx * p.seed_k + p.seed_k - 1];
+    if (w != PX_EMPTY) return cand_key(w);
+  }
+  return __int_as_float(0x7f800000);
+}
 
 // Approximate keys of 32 accumulator columns (base rows rbase ..): -q.x, or
 // ||x||^2 - 2 q.x with the row norms (padded to whole 256-row tiles, so every
@@ -205,7 +225,7 @@ __device__ __forceinline__ void insert_one(TopList<CAP>& T, float key, int64_t r
   const uint64_t cand = pack_cand(key, static_cast<uint32_t>(row));
   if (cand < T.thr) {
     list_insert<CAP>(T.L, T.thr, T.maxpos, cand);
-    T.thr_key = T.thr == PX_EMPTY ? __int_as_float(0x7f800000) : cand_key(T.thr);
+    T.thr_key = T.thr == PX_EMPTY ? T.open_key : cand_key(T.thr);
   }
 }
 
@@ -221,7 +241,7 @@ __device__ __forceinline__ void insert_passing(TopList<CAP>& T, uint32_t pass, c
       const uint64_t cand = pack_cand(kj, static_cast<uint32_t>(rbase + j));
       if (cand < T.thr) {
         list_insert<CAP>(T.L, T.thr, T.maxpos, cand);
-        T.thr_key = T.thr == PX_EMPTY ? __int_as_float(0x7f800000) : cand_key(T.thr);
+        T.thr_key = T.thr == PX_EMPTY ? T.open_key : cand_key(T.thr);
       }
     }
   }
@@ -385,7 +405,7 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
         const int qp = item % p.T;  // group of QT query tiles
         const int split = item / p.T;
-        const int t0 = split * p.tiles_per_split;
+        const int t0 = split * p.split_stride;
         const int t1 = min(p.nb, t0 + p.tiles_per_split);
         for (int t = t0; ok && t < t1; ++t) {
           for (int kc = 0; kc < KC; ++kc) {
@@ -427,7 +447,7 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       bool ok = true;
       for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
         const int split = item / p.T;
-        const int t0 = split * p.tiles_per_split;
+        const int t0 = split * p.split_stride;
         const int t1 = min(p.nb, t0 + p.tiles_per_split);
         for (int t = t0; ok && t < t1; ++t) {
           if (!tc::mbar_wait(tempty_bar(acc), acc_phase ^ 1, s_abort)) {
@@ -503,14 +523,11 @@ gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
       const int qp = item % p.T;
       const int split = item / p.T;
-      const int t0 = split * p.tiles_per_split;
+      const int t0 = split * p.split_stride;
       const int t1 = min(p.nb, t0 + p.tiles_per_split);
       const int64_t qidx = static_cast<int64_t>(qp * QT + wg) * BM + row_in_tile;
-      // +inf: accept everything at first. A padding query row (past nq) has
-      // all-zero products, hence equal keys that would all pass and take
-      // the rare insertion path on every step: -inf lets nothing in.
       TopList<CAP> T;
-      T.reset(__int_as_float(qidx < p.nq ? 0x7f800000 : 0xff800000));
+      T.reset(list_start_key(p, qidx));
       for (int t = t0; t < t1; ++t) {
         // Warp-uniform decision: the tcgen05.ld below is .sync.aligned.
         const bool got = __all_sync(0xffffffffu, tc::mbar_wait(tfull_bar(acc), acc_phase, s_abort));
@@ -660,7 +677,7 @@ gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       for (int item = cluster; ok && item < p.n_items; item += nclusters) {
         const int qg = item % p.T;
         const int split = item / p.T;
-        const int t0 = split * p.tiles_per_split;
+        const int t0 = split * p.split_stride;
         const int t1 = min(p.nb, t0 + p.tiles_per_split);
         for (int t = t0; ok && t < t1; ++t) {
           for (int kc = 0; kc < KC; ++kc) {
@@ -702,7 +719,7 @@ gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       bool ok = true;
       for (int item = cluster; ok && item < p.n_items; item += nclusters) {
         const int split = item / p.T;
-        const int t0 = split * p.tiles_per_split;
+        const int t0 = split * p.split_stride;
         const int t1 = min(p.nb, t0 + p.tiles_per_split);
         for (int t = t0; ok && t < t1; ++t) {
           if (!tc::mbar_wait(tempty_bar(acc), acc_phase ^ 1, s_abort)) {
@@ -756,14 +773,12 @@ gemm_topk_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     for (int item = cluster; ok && item < p.n_items; item += nclusters) {
       const int qg = item % p.T;
       const int split = item / p.T;
-      const int t0 = split * p.tiles_per_split;
+      const int t0 = split * p.split_stride;
       const int t1 = min(p.nb, t0 + p.tiles_per_split);
       const int64_t qidx = static_cast<int64_t>(qg) * (2 * PM) + static_cast<int64_t>(rank) * PM + row_in_tile;
-      // +inf: accept everything at first; -inf for a padding query row (see
-      // gemm_topk_kernel). Two lists, over alternate 32-column blocks: the
-      // same number of insertions as one list of twice the size, each at
-      // half the cost.
-      const float start_key = __int_as_float(qidx < p.nq ? 0x7f800000 : 0xff800000);
+      // Two lists, over alternate 32-column blocks: the same number of
+      // insertions as one list of twice the size, each at half the cost.
+      const float start_key = list_start_key(p, qidx);
       TopList<CAP> TA, TB;
       TA.reset(start_key);
       TB.reset(start_key);

@@ -7,8 +7,10 @@
 // are the answer -- provided no row outside the candidate set can beat the
 // k-th. That is certified with a rigorous bound eps on |approx - exact|:
 //   every non-candidate x has approx(x) >= A, the largest approximate key
-//   among the candidates, hence exact(x) >= A - eps; the result is exact if
-//   exact_k < A - eps (strict, so no outside row can even tie).
+//   among the candidates (or less: the largest key of a full split list, or
+//   the starting threshold of a seeded pass), hence exact(x) >= A - eps; the
+//   result is exact if exact_k < A - eps (strict, so no outside row can even
+//   tie).
 // A query whose certificate fails is listed for the exact streaming scan.
 //
 // eps is a worst-case bound, evaluated in double precision, with three parts.
@@ -150,6 +152,12 @@ rescore_kernel(const RescoreArgs a) {
       m = o < m ? o : m;
     }
     last = m < last ? m : last;
+  }
+  // A seeded pass admitted only keys <= its starting threshold: every row it
+  // left out has a larger approximate key.
+  if (a.seed != nullptr) {
+    const uint64_t s = a.seed[q * a.seed_k + a.seed_k - 1];
+    last = s < last ? s : last;
   }
 
   // Exact keys, four candidates at a time, in approximate-key order: thread l

@@ -429,6 +429,15 @@ PX_API px_status px_flat_set_path(px_flat* h, int32_t mode) {
   return PX_OK;
 }
 
+PX_API px_status px_flat_set_sample_pass(px_flat* h, int32_t mode) {
+  px_status s = flat_check(h);
+  if (s != PX_OK) return s;
+  if (mode != PX_SAMPLE_AUTO && mode != PX_SAMPLE_OFF && mode != PX_SAMPLE_ON)
+    return set_error(PX_EINVAL, "sample pass mode must be PX_SAMPLE_AUTO, PX_SAMPLE_OFF or PX_SAMPLE_ON");
+  h->sample_mode = mode;
+  return PX_OK;
+}
+
 PX_API void px_set_profiling(int32_t enable) { g_profiling = enable ? 1 : 0; }
 
 PX_API int64_t px_launch_count(void) { return g_launches.load(); }
@@ -443,6 +452,7 @@ PX_API px_status px_flat_last_profile(const px_flat* h, px_search_profile* out) 
   out->fallback_queries = sh.last_fallback;
   out->refined_queries = sh.last_refined;
   out->first_pass = sh.last_pass;
+  out->sample_tiles = sh.last_sample_tiles;
   out->profiled = 0;
   out->main_kernel_ms = 0.f;
   if (sh.last_profiled) {
@@ -706,6 +716,7 @@ static px_status flat_search_replay(px_flat* h, FlatShard& sh, const SearchPlan&
   sh.last_fallback = 0;
   sh.last_refined = 0;
   sh.last_pass = -1;
+  sh.last_sample_tiles = 0;
   sh.last_launches = 3;
   sh.last_profiled = false;
   std::memcpy(out_ids, pin + q_al, obytes * sizeof(int64_t));

@@ -135,6 +135,8 @@ struct GemmTopkArgs {
   int T;                // groups of gemm_qt_for(k) query tiles of 128
   int S;                // base splits
   int tiles_per_split;  // base tiles of gemm_bn_for(k) rows per split
+  int split_stride;     // base tiles from one split's first tile to the next's
+                        // (tiles_per_split, or more for a strided sample)
   int nb;               // base tiles
   int n_items;          // T * S
   bool l2;
@@ -144,6 +146,11 @@ struct GemmTopkArgs {
   uint64_t* partial;    // [nq][S][cap] sorted approximate candidates
   int* err;             // device word raised on a timed-out wait
   const uint32_t* mask_bits;  // optional filter, one bit per row (1 = may be returned)
+  // Optional starting threshold per query ([nq][seed_k] sorted words of a
+  // sample pass, seed_k >= k; its last word's key): the lists admit only
+  // keys <= it. Null: every list starts open.
+  const uint64_t* seed;
+  int seed_k;
 };
 // Packs a byte mask (nonzero = keep) into one bit per row, 32 rows per word.
 cudaError_t launch_pack_mask(const uint8_t* mask, int64_t n, uint32_t* bits, cudaStream_t stream);
@@ -187,6 +194,8 @@ struct RescoreArgs {
   const int* q_lo_flag;
   int pass_kind;           // PassKind of the candidate pass
   int norm_folded;         // L2 keys came from bf16 rows carrying ||x||^2 (2 q.x - ||x||^2)
+  const uint64_t* seed;    // [nq][seed_k] the candidate pass's starting thresholds, or null
+  int seed_k;
   uint64_t* out;           // [nq][k] exact candidates
   int* status;             // [nq] 0 = certified
   int* n_fail;             // count of uncertified queries

@@ -495,6 +495,7 @@ PX_API px_status px_pq_last_profile(const px_pq* h, px_search_profile* out) {
   out->fallback_queries = 0;
   out->refined_queries = 0;
   out->first_pass = -1;
+  out->sample_tiles = 0;
   out->profiled = 0;
   out->main_kernel_ms = 0.f;
   if (sh.last_profiled) {

@@ -104,6 +104,7 @@ struct FlatShard {
   cudaEvent_t ev_start = nullptr, ev_stop = nullptr;  // brackets the dominant kernel when profiling
   cudaEvent_t ev_done = nullptr;  // this shard's results are in the gather buffer (own device)
   int last_path = 0, last_fallback = 0, last_refined = 0, last_launches = 0, last_pass = -1;
+  int last_sample_tiles = 0;
   bool last_profiled = false;
   px::Segments segs;
   px::DevBuf ws;           // search workspace
@@ -152,6 +153,7 @@ struct px_flat {
   int64_t total = 0;
   int64_t id_offset = 0;
   int path_mode = PX_PATH_AUTO;
+  int sample_mode = PX_SAMPLE_AUTO;
   std::vector<FlatShard> shards;
   GatherBuf gather;
   px::HostBuf pinned;  // staging for pageable host buffers
@@ -172,7 +174,8 @@ struct SearchPlan {
   int64_t rows_per_cta = 0;
   // tensor-core path
   int cap = 0, cands = 0, T = 0, S = 0, nb = 0, tiles_per_split = 0, n_items = 0, grid = 0;
-  int lists = 0;  // candidate lists per query: S, or 2 * S on CTA pairs
+  int lists = 0;  // candidate lists per query: S, or 4 * S on CTA pairs
+  int seed_S = 0;  // single-tile splits of the bf16 pass's sample pass (0: none)
   int64_t q_rows = 0;
   size_t ws_bytes = 0;
   uint64_t* partial = nullptr;

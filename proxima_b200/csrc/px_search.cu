@@ -28,6 +28,12 @@ namespace {
 
 constexpr int kGemmMinQueries = 16;
 constexpr int kGemmMinRows = 4096;
+// The bf16 pass's sample pass: this many single base tiles spread evenly over
+// the shard (8,192 rows), taken when the shard holds at least four times as
+// many tiles and (PX_SAMPLE_AUTO) its splits are at least kSeedMinSplitTiles
+// long.
+constexpr int kSeedSplits = 32;
+constexpr int kSeedMinSplitTiles = 512;
 
 int64_t gcd64(int64_t a, int64_t b) {
   while (b) {
@@ -42,7 +48,7 @@ int64_t gcd64(int64_t a, int64_t b) {
 
 // Work split of one tensor-core candidate pass over nq queries. Workers are
 // the persistent CTAs (one per SM), or CTA pairs for the bf16 pass.
-static void plan_gemm(const FlatShard& sh, int64_t nq, int k, PassKind kind, SearchPlan& plan) {
+static void plan_gemm(const FlatShard& sh, int64_t nq, int k, PassKind kind, int sample_mode, SearchPlan& plan) {
   plan.path = FlatPath::Gemm;
   const bool pair = kind == kPassBf16;
   plan.cap = pair ? gemm_pair_cap(k) : gemm_cap_for(k);
@@ -76,6 +82,23 @@ static void plan_gemm(const FlatShard& sh, int64_t nq, int k, PassKind kind, Sea
   plan.n_items = static_cast<int>(T * S);
   plan.grid = static_cast<int>(pair ? 2 * std::min<int64_t>(workers, T * S) : std::min<int64_t>(workers, T * S));
   plan.q_rows = T * group_rows;
+  // Sample pass: each list of a fresh split accepts every row until it holds
+  // CAP of them and then refills about CAP * (1 + ln(rows / CAP)) times. A
+  // first pass over a strided sample of kSeedSplits tiles gives every query
+  // the cands-th best key among 8,192 rows, and the main pass's lists admit
+  // only keys at or below it. The cands-th, not the k-th: that key also
+  // bounds the certificate, and the merged candidates' own bound is their
+  // cands-th key, so the start costs the certificate nothing (on clustered
+  // data the sample's k-th key lies within the bf16 error of the true k-th).
+  // It pays on long splits (config 5: 269 -> 259 ms; config 4 unchanged).
+  // On short ones (configs 1, 2) it costs more than it saves: their lists
+  // still refill often enough that nearly every 32-column block has some
+  // lane of the warp on the insertion path, while the sample pass and its
+  // merge add a fixed 20-50 us.
+  const bool seed_ok = pair && nb >= 4 * kSeedSplits;
+  plan.seed_S = 0;
+  if (seed_ok && (sample_mode == PX_SAMPLE_ON || (sample_mode == PX_SAMPLE_AUTO && tps >= kSeedMinSplitTiles)))
+    plan.seed_S = kSeedSplits;
 }
 
 namespace {
@@ -85,6 +108,8 @@ struct TensorWs {
   float* q_hl = nullptr;            // query split plane, q_rows x 2*ld (tf32 passes)
   void* qb = nullptr;               // query bf16 plane, q_rows x ldb (bf16 pass)
   uint64_t* partial = nullptr;      // [nq][S][cap] per-split lists
+  uint64_t* seed_partial = nullptr; // [nq][4 * seed_S][cap] the sample pass's lists
+  uint64_t* seed = nullptr;         // [nq][cands] their merged best: the main pass's thresholds
   uint64_t* merged = nullptr;       // [nq][cands]
   uint64_t* final_cands = nullptr;  // [nq][k] exact candidates
   int* status = nullptr;            // [nq]
@@ -108,6 +133,11 @@ void carve_tensor_ws(Carver& c, const SearchPlan& plan, int64_t nq, int ld, int 
   else
     w.q_hl = static_cast<float*>(c.take(sizeof(float) * static_cast<size_t>(plan.q_rows) * 2 * ld));
   w.partial = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.lists * plan.cap));
+  if (kind == kPassBf16 && plan.seed_S > 0) {
+    w.seed_partial =
+        static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * 4 * plan.seed_S * plan.cap));
+    w.seed = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.cands));
+  }
   w.merged = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * plan.cands));
   w.final_cands = static_cast<uint64_t*>(c.take(sizeof(uint64_t) * static_cast<size_t>(nq) * k));
   w.status = static_cast<int*>(c.take(sizeof(int) * static_cast<size_t>(nq)));
@@ -140,7 +170,7 @@ px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, in
   Carver c;
   if (gemm) {
     const PassKind first = first_pass_for(h, k);
-    plan_gemm(sh, nq, k, first, plan);
+    plan_gemm(sh, nq, k, first, h->sample_mode, plan);
     TensorWs w;
     carve_tensor_ws(c, plan, nq, h->ld, h->ldb, k, first, w);
     if (masked) c.take(sizeof(uint32_t) * mask_words(sh.n));
@@ -262,6 +292,7 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
   g.T = plan.T;
   g.S = plan.S;
   g.tiles_per_split = plan.tiles_per_split;
+  g.split_stride = plan.tiles_per_split;
   g.nb = plan.nb;
   g.n_items = plan.n_items;
   g.l2 = l2 && !folded;
@@ -271,7 +302,29 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
   g.partial = w.partial;
   g.err = w.counters + 2;
   g.mask_bits = mask_bits;
+  g.seed = nullptr;
+  g.seed_k = plan.cands;
+  const bool seeded = w.seed != nullptr;
   if (profile_main) cudaEventRecord(sh.ev_start, stream);
+  if (seeded) {
+    // The sample pass: one tile per split, the splits kSeedSplits evenly
+    // spaced tiles apart, same kernel and filter; then the cands best words
+    // of its lists per query.
+    GemmTopkArgs gs = g;
+    gs.S = plan.seed_S;
+    gs.tiles_per_split = 1;
+    gs.split_stride = plan.nb / plan.seed_S;
+    gs.n_items = plan.T * plan.seed_S;
+    gs.partial = w.seed_partial;
+    const int seed_grid =
+        2 * static_cast<int>(std::min<int64_t>(gemm_pair_clusters(sh.device), static_cast<int64_t>(gs.n_items)));
+    e = launch_gemm_topk(gs, w.qb, plan.q_rows, sh.xb, kind, seed_grid, stream);
+    if (e != cudaSuccess) return cuda_status(e, "tensor-core sample pass launch");
+    e = launch_merge_lists(w.seed_partial, nq, 4 * plan.seed_S, plan.cap, plan.cands, w.seed, stream);
+    if (e != cudaSuccess) return cuda_status(e, "sample merge launch");
+    g.seed = w.seed;
+    g_launches += 2;
+  }
   if (kind == kPassBf16)
     e = launch_gemm_topk(g, w.qb, plan.q_rows, sh.xb, kind, plan.grid, stream);
   else
@@ -299,6 +352,8 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
   r.q_lo_flag = w.counters + 1;
   r.pass_kind = kind;
   r.norm_folded = folded ? 1 : 0;
+  r.seed = g.seed;
+  r.seed_k = plan.cands;
   r.out = w.final_cands;
   r.status = w.status;
   r.n_fail = w.counters;
@@ -326,6 +381,7 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   sh.last_fallback = 0;
   sh.last_refined = 0;
   sh.last_pass = -1;
+  sh.last_sample_tiles = 0;
   sh.last_profiled = prof;
   const int64_t launches0 = g_launches.load();
   Carver c(ws ? ws : sh.ws.ptr);
@@ -347,6 +403,7 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   // 3. Whatever is still uncertified goes through the exact scan.
   const PassKind first = first_pass_for(h, k);
   sh.last_pass = first;
+  sh.last_sample_tiles = first == kPassBf16 ? plan.seed_S : 0;
   TensorWs w;
   carve_tensor_ws(c, plan, nq, h->ld, h->ldb, k, first, w);
   plan.final_cands = w.final_cands;
@@ -362,7 +419,7 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
   if (n_fail > 0) {
     if (first != kPass3xTf32 && inexact && refine_pays(n_fail, k)) {
       SearchPlan p2;
-      plan_gemm(sh, n_fail, k, kPass3xTf32, p2);
+      plan_gemm(sh, n_fail, k, kPass3xTf32, h->sample_mode, p2);
       Carver c2;
       c2.take(sizeof(float) * static_cast<size_t>(n_fail) * h->dim);
       TensorWs w2;
@@ -409,7 +466,7 @@ px_status first_pass_candidates(const px_flat* h, FlatShard& sh, int metric, con
   if (nq > (int64_t(1) << 30)) return set_error(PX_EUNSUPPORTED, "too many queries in one call");
   const PassKind kind = first_pass_for(h, k);
   SearchPlan plan;
-  plan_gemm(sh, nq, k, kind, plan);
+  plan_gemm(sh, nq, k, kind, h->sample_mode, plan);
   Carver c;
   TensorWs w;
   carve_tensor_ws(c, plan, nq, h->ld, h->ldb, k, kind, w);

@@ -129,3 +129,4 @@ def test_record_layout_and_new_entry_points_validate_without_gpu(px):
     assert lib.px_flat_debug_candidates(None, None, 1, 10, 64, None, None, ctypes.byref(cands),
                                         ctypes.byref(kind)) == px._lib.PX_EINVAL
     assert lib.px_pq_search_device(None, None, 1, 10, 0, None, None, None) == px._lib.PX_EINVAL
+    assert lib.px_flat_set_sample_pass(None, 0) == px._lib.PX_EINVAL

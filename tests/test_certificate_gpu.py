@@ -116,6 +116,36 @@ def test_tensor_path_certificate_adversarial_mixed_batch(pxm):
     _parity.check_flat(data, O.IP, queries, ids, d, 10)
 
 
+@pytest.mark.parametrize("metric", [O.IP, O.L2])
+def test_tensor_path_certificate_adversarial_sample_pass(pxm, metric):
+    """The same decoys on a shard long enough for the sample pass (160
+    tiles; the sample is tiles 0, 5, ..., 155). The decoys sit in sample tile
+    0, so every query starts from the 64th decoy's bf16 key (64 candidates
+    are rescored for k = 10), and the true best row (in tile 3, outside the
+    sample) scores above it in bf16: the main pass never offers it. The
+    certificate's bound is then the starting key itself, which the decoys'
+    exact keys do not clear, so the query must leave the bf16 tier, and the
+    answer must still be the oracle's."""
+    n = 40960
+    if metric == O.IP:
+        small, queries = _adversarial_ip()
+    else:
+        small, queries = _adversarial_folded_l2()
+    d = small.shape[1]
+    data = np.zeros((n, d), dtype=np.float32)
+    data[:200] = small[:200]
+    true_row = 3 * 256 + 7
+    data[true_row] = small[200]
+    idx = _index(pxm, data, metric)
+    idx.set_sample_pass("on")
+    ids, dd = idx.search_batch(queries, k=10)
+    prof = idx.last_search_profile()
+    assert prof["first_pass"] == "bf16" and prof["sample_tiles"] == 32, prof
+    assert prof["fallback_queries"] + prof["refined_queries"] == len(queries), prof
+    assert np.all(ids[:, 0] == true_row), ids[:, :3]
+    _parity.check_flat(data, metric, queries, ids, dd, 10)
+
+
 # ---- the accumulation model --------------------------------------------------
 
 def _bf16_exact(rng, shape, lo, hi):

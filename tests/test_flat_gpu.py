@@ -485,3 +485,98 @@ def test_small_batch_graph_replay(pxm):
     # A query equal to a base row finds it at distance 0 in the grown index.
     ids, d = idx.search(data[4321], k=3)
     assert ids[0] == 4321 and d[0] == 0.0
+
+
+# ---- the bf16 pass's sample pass ----------------------------------------------
+# The bf16 pass can first run over 32 single tiles spread evenly over the
+# shard; the 64th (k <= 16), 128th or 256th best key each query finds there is
+# where its lists start, and rows above it are never offered. By default only
+# shards with splits of 512+ tiles (millions of rows) take it; these tests
+# force it on shards of 128+ tiles.
+
+def _run_sampled(pxm, data, metric, queries, k, mode="on"):
+    idx = pxm.FlatIndex(data.shape[1], _metric(pxm, metric))
+    idx.add(data)
+    idx.set_search_path("tensor")
+    idx.set_sample_pass(mode)
+    ids, d = idx.search_batch(queries, k=k)
+    return ids, d, idx.last_search_profile()
+
+
+@pytest.mark.parametrize("metric,dim,nq,k", [
+    (O.IP, 64, 300, 10),    # two 8-entry lists per thread
+    (O.L2, 96, 257, 10),    # folded norms in the padding
+    (O.L2, 128, 64, 16),    # folded norms in one more K slice
+    (O.IP, 384, 130, 1),
+    (O.L2, 320, 100, 40),   # norm epilogue (dim > 256), 16-entry lists
+    (O.IP, 48, 48, 100),    # the largest k of the bf16 pass
+])
+def test_tensor_path_sample_pass_parity(pxm, metric, dim, nq, k):
+    n = 40000
+    if metric == O.IP:
+        data, queries = _data.unit_gaussian(n, dim, dim + 1), _data.unit_gaussian(nq, dim, dim + 2)
+    else:
+        data, queries = _data.gaussian_mixture(n, nq, d=dim, centres=200, seed=dim)
+    ids, d, prof = _run_sampled(pxm, data, metric, queries, k)
+    assert prof["first_pass"] == "bf16" and prof["sample_tiles"] == 32, prof
+    _parity.check_flat(data, metric, queries, ids, d, k)
+    # The clustered L2 cases leave some queries to the exact scan whether
+    # or not the sample pass runs (11 of 64 and 11 of 100 here both ways:
+    # the lists start from the sample's 64th or 128th key, above the merged
+    # candidates' own bound).
+    assert prof["fallback_queries"] <= max(4, nq // (10 if metric == O.IP else 5)), prof
+
+
+def test_tensor_path_sample_pass_modes(pxm):
+    short = _data.unit_gaussian(127 * 256, 32, 3)  # one tile short of the sample pass
+    queries = _data.unit_gaussian(40, 32, 4)
+    ids, d, prof = _run_sampled(pxm, short, O.IP, queries, 10, "on")
+    assert prof["sample_tiles"] == 0, prof
+    _parity.check_flat(short, O.IP, queries, ids, d, 10)
+    data = _data.unit_gaussian(40000, 32, 5)  # 157 tiles in splits of a few tiles
+    for mode, tiles in (("auto", 0), ("off", 0), ("on", 32)):
+        ids, d, prof = _run_sampled(pxm, data, O.IP, queries, 10, mode)
+        assert prof["sample_tiles"] == tiles, (mode, prof)
+        _parity.check_flat(data, O.IP, queries, ids, d, 10)
+    idx = pxm.FlatIndex(32)
+    with pytest.raises(pxm.PxError, match="sample pass mode"):
+        pxm._lib.check(pxm._lib.load().px_flat_set_sample_pass(idx.handle, 7))
+
+
+@pytest.mark.parametrize("metric", [O.L2, O.IP])
+def test_tensor_path_sample_pass_filtered(pxm, metric):
+    # 160 tiles: the sample is tiles 0, 5, 10, ..., 155. The filter applies
+    # to both passes: admitted rows only inside the sample, only outside it,
+    # fewer than k, or none (a query whose sample holds fewer than k rows
+    # starts with open lists).
+    n, dim, nq, k = 40960, 64, 64, 10
+    data = _data.unit_gaussian(n, dim, 51)
+    queries = _data.unit_gaussian(nq, dim, 52)
+    idx = pxm.FlatIndex(dim, _metric(pxm, metric))
+    idx.add(data)
+    idx.set_search_path("tensor")
+    idx.set_sample_pass("on")
+    tile = np.arange(n) // 256
+    rng = np.random.default_rng(53)
+    masks = [rng.random(n) < 0.3,
+             np.arange(n) < 256,                      # sample tile 0 only
+             tile % 5 != 0,                           # every tile but the sample's
+             (tile % 5 == 3) & (rng.random(n) < 0.01),
+             np.isin(np.arange(n), [7, 20000, 40959]),
+             np.zeros(n, bool)]
+    for mask in masks:
+        ids, d = idx.search_batch_filtered(queries, mask, k=k)
+        assert idx.last_search_profile()["sample_tiles"] == 32
+        _parity.check_flat(data, metric, queries, ids, d, k, filter_=mask)
+
+
+def test_tensor_path_sample_pass_ties(pxm):
+    # Every row 40 times over 48,000 rows: the sample's k-th key is shared by
+    # rows outside the sample, which are admitted too (a key equal to the
+    # starting one passes), and the ties exceed the lists.
+    base = _data.unit_gaussian(1200, 64, 61)
+    data = np.repeat(base, 40, axis=0)
+    queries = _data.unit_gaussian(32, 64, 62)
+    ids, d, prof = _run_sampled(pxm, data, O.IP, queries, 10)
+    assert prof["sample_tiles"] == 32, prof
+    _parity.check_flat(data, O.IP, queries, ids, d, 10)
