@@ -20,21 +20,47 @@ constexpr size_t kMergeStageBytes = 40 * 1024;
 // From this many output words on, the merge selects by value search
 // (merge_select_kernel) rather than popping one word per tournament step.
 constexpr int kMergeSelectMinK = 128;
+// Shared memory the threshold merge (merge_heads_kernel) may take per block.
+constexpr size_t kMergeHeadsMaxSmem = 200 * 1024;
 
-// Copies n words to shared memory, eight loads in flight per lane (a plain
+// Copies n words to shared memory, 16 loads in flight per lane (a plain
 // load-store loop would wait out a global-memory latency per word).
 __device__ __forceinline__ void stage_words(uint64_t* dst, const uint64_t* __restrict__ src, int n, int lane) {
-  for (int i0 = 0; i0 < n; i0 += 32 * 8) {
-    uint64_t v[8];
+  constexpr int kInFlight = 16;
+  for (int i0 = 0; i0 < n; i0 += 32 * kInFlight) {
+    uint64_t v[kInFlight];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
+    for (int u = 0; u < kInFlight; ++u) {
       const int i = i0 + u * 32 + lane;
       v[u] = i < n ? __ldg(src + i) : 0ull;
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
+    for (int u = 0; u < kInFlight; ++u) {
       const int i = i0 + u * 32 + lane;
       if (i < n) dst[i] = v[u];
+    }
+  }
+}
+
+// Ascending bitonic sort of n words (a power of two, at least 2) in shared
+// memory by one warp. (Loading all of a lane's pairs of a stage before
+// storing any, in registers sized for n = 1,024, measured slower: it cut
+// the warps per SM and did the largest sort's work for every n.)
+__device__ __forceinline__ void warp_bitonic_sort(uint64_t* a, int n, int lane) {
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int p = lane; p < n / 2; p += 32) {
+        // Pair p: positions lo_i, lo_i + stride (stride a power of two).
+        const int lo_i = ((p & ~(stride - 1)) << 1) | (p & (stride - 1));
+        const int hi_i = lo_i + stride;
+        const bool up = (lo_i & size) == 0;
+        const uint64_t x = a[lo_i], y = a[hi_i];
+        if ((x > y) == up) {
+          a[lo_i] = y;
+          a[hi_i] = x;
+        }
+      }
+      __syncwarp();
     }
   }
 }
@@ -125,6 +151,65 @@ __device__ __forceinline__ int count_le_sorted(const uint64_t* L, int len, uint6
   return lo;
 }
 
+// One warp per query: the k smallest words of `nlists` sorted lists by a
+// threshold instead of a k-step tournament (whose k dependent warp
+// reductions dominate small searches). The query's lists are staged in shared
+// memory and their heads sorted; H, the k-th smallest head, bounds the
+// answer, since k distinct words (those heads) are <= H. Only the lists whose
+// head is <= H can hold words <= H -- exactly k lists, the words of a query
+// being distinct -- so at most min(nlists, k) * list_len words qualify; they
+// are gathered (exclusive scan of the lanes' counts) and sorted, and the
+// first k are the answer. With fewer than k lists (or fewer than k non-empty
+// ones) every real word qualifies. Shared memory per warp: the staged lists,
+// hp words of heads and cp words of gathered candidates (powers of two, at
+// most 1,024).
+__global__ void __launch_bounds__(kMergeWarps * 32)
+merge_heads_kernel(const uint64_t* __restrict__ lists, int64_t nq, int nlists, int list_len, int k, int hp,
+                   int cp, uint64_t* __restrict__ out) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = nlists * list_len;
+  uint64_t* stage = reinterpret_cast<uint64_t*>(smem_raw) + static_cast<size_t>(warp) * (total + hp + cp);
+  uint64_t* heads = stage + total;
+  uint64_t* cand = heads + hp;
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * kMergeWarps + warp;
+  if (q >= nq) return;
+  stage_words(stage, lists + q * static_cast<int64_t>(total), total, lane);
+  __syncwarp();
+  uint64_t H = PX_EMPTY;
+  if (nlists >= k) {
+    for (int l = lane; l < hp; l += 32) heads[l] = l < nlists ? stage[l * list_len] : PX_EMPTY;
+    __syncwarp();
+    warp_bitonic_sort(heads, hp, lane);
+    H = heads[k - 1];
+  }
+  // PX_EMPTY is the largest word: with H == PX_EMPTY count the real words.
+  const uint64_t lim = H == PX_EMPTY ? PX_EMPTY - 1 : H;
+  int mine = 0;
+  for (int l = lane; l < nlists; l += 32) mine += count_le_sorted(stage + l * list_len, list_len, lim);
+  int incl = mine;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += o;
+  }
+  // <= cp by the argument above; the clamps only keep a violation of it
+  // inside the buffer.
+  const int count = min(__shfl_sync(0xffffffffu, incl, 31), cp);
+  int at = incl - mine;
+  for (int l = lane; l < nlists; l += 32) {
+    const uint64_t* L = stage + l * list_len;
+    const int c = count_le_sorted(L, list_len, lim);
+    for (int i = 0; i < c && at < cp; ++i) cand[at++] = L[i];
+  }
+  int n2 = 32;
+  while (n2 < count) n2 <<= 1;
+  for (int i = count + lane; i < n2; i += 32) cand[i] = PX_EMPTY;
+  __syncwarp();
+  warp_bitonic_sort(cand, n2, lane);
+  for (int j = lane; j < k; j += 32) out[q * k + j] = j < n2 ? cand[j] : PX_EMPTY;
+}
+
 // One warp per query, for large k: the k smallest words of `nlists` sorted
 // lists, without a k-step tournament. The query's lists are staged in shared
 // memory; the k-th smallest word T is found bit by bit, counting the words
@@ -192,22 +277,7 @@ merge_select_kernel(const uint64_t* __restrict__ lists, int64_t nq, int nlists, 
   __syncwarp();
   for (int i = kk + lane; i < kp; i += 32) sel[i] = PX_EMPTY;
   __syncwarp();
-  // Bitonic sort of kp (a power of two) words, ascending.
-  for (int size = 2; size <= kp; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int p = lane; p < kp / 2; p += 32) {
-        const int lo_i = 2 * stride * (p / stride) + (p % stride);
-        const int hi_i = lo_i + stride;
-        const bool up = (lo_i & size) == 0;
-        const uint64_t a = sel[lo_i], b = sel[hi_i];
-        if ((a > b) == up) {
-          sel[lo_i] = b;
-          sel[hi_i] = a;
-        }
-      }
-      __syncwarp();
-    }
-  }
+  warp_bitonic_sort(sel, kp, lane);  // kp: a power of two, 128 .. 1,024
   for (int j = lane; j < k; j += 32) out[q * k + j] = sel[j];
 }
 
@@ -283,6 +353,23 @@ cudaError_t launch_merge_lists(const uint64_t* lists, int64_t nq, int nlists, in
       (static_cast<size_t>(kMergeWarps) * nlists * (sizeof(uint64_t) + sizeof(int)) + 15) & ~size_t(15);
   const size_t stage = sizeof(uint64_t) * static_cast<size_t>(nlists) * list_len;
   const bool staged = stage <= kMergeStageBytes;
+  // Threshold merge: heads and gathered candidates each at most 1,024 words.
+  {
+    int hp = 32, cp = 32;
+    while (hp < nlists) hp <<= 1;
+    const int64_t cmax = static_cast<int64_t>(nlists < k ? nlists : k) * list_len;
+    while (cp < cmax) cp <<= 1;
+    const size_t hsmem = static_cast<size_t>(kMergeWarps) * (stage + sizeof(uint64_t) * (hp + cp));
+    if (staged && list_len > 0 && hp <= 1024 && cp <= 1024 && hsmem <= kMergeHeadsMaxSmem) {
+      cudaError_t e = cudaFuncSetAttribute(merge_heads_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(hsmem));
+      if (e != cudaSuccess) return e;
+      const int64_t blocks = (nq + kMergeWarps - 1) / kMergeWarps;
+      merge_heads_kernel<<<static_cast<unsigned>(blocks), kMergeWarps * 32, hsmem, stream>>>(
+          lists, nq, nlists, list_len, k, hp, cp, out);
+      return cudaGetLastError();
+    }
+  }
   // Large k: select by value search instead of a k-step tournament.
   if (staged && k >= kMergeSelectMinK && k <= 1024) {
     int kp = 1;

@@ -59,8 +59,31 @@ namespace {
 
 constexpr int kRescoreWarps = 4;
 constexpr int kMaxCands = 256;
+// Candidate rows staged per warp and round: as many as fit in ~16 KB, a
+// multiple of four between 4 and 16 (one 4-candidate step per 8-lane group).
+// Rows too long for 8 of them (d > 480) are not staged: four rows per round
+// is what the direct loads already keep in flight, and the staging area
+// would only cut the warps per SM.
+constexpr int kRowStageBytes = 16 * 1024;
 
-template <bool L2>
+// Floats per staged row: d rounded up to 32, plus 8, so the four rows of a
+// step start in four different 8-bank slices.
+__host__ __device__ __forceinline__ int staged_row_floats(int d) { return ((d + 31) & ~31) + 8; }
+__host__ __device__ __forceinline__ int staged_rows(int d) {
+  const int g = (kRowStageBytes / (4 * staged_row_floats(d))) & ~3;
+  return g < 4 ? 4 : (g > 16 ? 16 : g);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// STAGE: candidate rows go through shared memory (below); otherwise (rows too
+// long for it) each lane fetches kBatch of its elements before adding them.
+template <bool L2, bool STAGE>
 __global__ void __launch_bounds__(kRescoreWarps * 32)
 rescore_kernel(const RescoreArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -70,6 +93,12 @@ rescore_kernel(const RescoreArgs a) {
   uint64_t* s_c = reinterpret_cast<uint64_t*>(reinterpret_cast<float*>(smem_raw) + kRescoreWarps * dq) +
                   warp * 2 * kMaxCands;
   uint64_t* s_sorted = s_c + kMaxCands;
+  const int ds = staged_row_floats(a.d);
+  const int G = STAGE ? staged_rows(a.d) : 4;
+  float* s_rows = reinterpret_cast<float*>(reinterpret_cast<uint64_t*>(reinterpret_cast<float*>(smem_raw) +
+                                                                       kRescoreWarps * dq) +
+                                           kRescoreWarps * 2 * kMaxCands) +
+                  static_cast<size_t>(warp) * G * ds;
   const int64_t q = static_cast<int64_t>(blockIdx.x) * kRescoreWarps + warp;
   if (q >= a.nq) return;
 
@@ -166,6 +195,10 @@ rescore_kernel(const RescoreArgs a) {
   // accumulator is the same sequential chain as the reference's, and the
   // group reads 32 contiguous bytes of the row per step. The lanes are then
   // summed left to right and the remainder added, as distance.rs does.
+  // The rows are random gathers: G of them at a time are copied to shared
+  // memory with every 16-byte piece in flight at once (one memory latency
+  // per G candidates instead of one per four), and the chains read them
+  // there.
   // Early exit: once `done` candidates are scored, every unscored candidate
   // and every row outside the set has an approximate key >= a* = min(the
   // next candidate's, last), hence an exact key >= lower_bound(a*). If k
@@ -175,25 +208,43 @@ rescore_kernel(const RescoreArgs a) {
   const int chunks = a.d >> 3;
   int scored = a.cap;
   bool early = false;
+  const int pieces = (a.d + 3) >> 2;  // 16-byte pieces per row (rows are 128-byte aligned, ld >= d rounded to 32)
+  const uint32_t rows_addr = static_cast<uint32_t>(__cvta_generic_to_shared(s_rows));
   for (int j0 = 0; j0 < a.cap; j0 += 4) {
+    if (STAGE && j0 % G == 0) {
+      // Stage candidates j0 .. j0 + G - 1 (the ones that exist).
+      __syncwarp();  // the previous group's rows are no longer read
+      for (int i = lane; i < G * pieces; i += 32) {
+        const int r = i / pieces, pc = i - r * pieces;
+        const int jr = j0 + r;
+        const uint64_t cr = jr < a.cap ? mq[jr] : PX_EMPTY;
+        if (cr != PX_EMPTY)
+          cp_async16(rows_addr + static_cast<uint32_t>((r * ds + pc * 4) * 4),
+                     a.base + static_cast<int64_t>(cand_row(cr)) * a.ld + pc * 4);
+      }
+      cp_async_wait_all();
+      __syncwarp();
+    }
     const int j = j0 + grp;
     const uint64_t c = j < a.cap ? mq[j] : PX_EMPTY;
     const bool valid = c != PX_EMPTY;
     const uint32_t row = valid ? cand_row(c) : 0u;
-    const float* x = a.base + static_cast<int64_t>(row) * a.ld;
+    const float* x = STAGE ? s_rows + (j % G) * ds : a.base + static_cast<int64_t>(row) * a.ld;
     float acc = 0.f;
     if (valid) {
-      // The row is a random gather: fetch kBatch of this lane's elements
-      // before adding them in order, so kBatch loads are in flight per
-      // thread instead of the few an unrolled add chain exposes.
-      constexpr int kBatch = 48;
-      for (int c0 = 0; c0 < chunks; c0 += kBatch) {
-        float xv[kBatch];
+      if constexpr (STAGE) {
+#pragma unroll 8
+        for (int cc = 0; cc < chunks; ++cc) acc = __fadd_rn(acc, lane_term<L2>(s_q[cc * 8 + l], x[cc * 8 + l]));
+      } else {
+        constexpr int kBatch = 48;
+        for (int c0 = 0; c0 < chunks; c0 += kBatch) {
+          float xv[kBatch];
 #pragma unroll
-        for (int b = 0; b < kBatch; ++b) xv[b] = c0 + b < chunks ? __ldg(x + (c0 + b) * 8 + l) : 0.f;
+          for (int b = 0; b < kBatch; ++b) xv[b] = c0 + b < chunks ? __ldg(x + (c0 + b) * 8 + l) : 0.f;
 #pragma unroll
-        for (int b = 0; b < kBatch; ++b)
-          if (c0 + b < chunks) acc = __fadd_rn(acc, lane_term<L2>(s_q[(c0 + b) * 8 + l], xv[b]));
+          for (int b = 0; b < kBatch; ++b)
+            if (c0 + b < chunks) acc = __fadd_rn(acc, lane_term<L2>(s_q[(c0 + b) * 8 + l], xv[b]));
+        }
       }
     }
     float sum = __shfl_sync(0xffffffffu, acc, g0);
@@ -284,19 +335,20 @@ cudaError_t launch_rescore(const RescoreArgs& a, cudaStream_t stream) {
   if (a.nq == 0) return cudaSuccess;
   if (a.cap > kMaxCands || a.k > a.cap) return cudaErrorInvalidValue;
   const int dq = (a.d + 3) & ~3;
-  const size_t smem = sizeof(float) * kRescoreWarps * dq + sizeof(uint64_t) * kRescoreWarps * 2 * kMaxCands;
+  const size_t base_smem = sizeof(float) * kRescoreWarps * dq + sizeof(uint64_t) * kRescoreWarps * 2 * kMaxCands;
+  const size_t staged_smem =
+      base_smem + sizeof(float) * kRescoreWarps * staged_rows(a.d) * staged_row_floats(a.d);
+  // Rows are staged in 16-byte pieces (ld a multiple of 4, the base 16-byte
+  // aligned), when the staged rows fit.
+  const bool stage = a.ld % 4 == 0 && reinterpret_cast<uintptr_t>(a.base) % 16 == 0 && staged_rows(a.d) >= 8 &&
+                     staged_smem <= 200 * 1024;
+  const size_t smem = stage ? staged_smem : base_smem;
   const unsigned blocks = static_cast<unsigned>((a.nq + kRescoreWarps - 1) / kRescoreWarps);
-  if (a.l2) {
-    cudaError_t e = cudaFuncSetAttribute(rescore_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    rescore_kernel<true><<<blocks, kRescoreWarps * 32, smem, stream>>>(a);
-  } else {
-    cudaError_t e = cudaFuncSetAttribute(rescore_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    rescore_kernel<false><<<blocks, kRescoreWarps * 32, smem, stream>>>(a);
-  }
+  auto kern = a.l2 ? (stage ? rescore_kernel<true, true> : rescore_kernel<true, false>)
+                   : (stage ? rescore_kernel<false, true> : rescore_kernel<false, false>);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  kern<<<blocks, kRescoreWarps * 32, smem, stream>>>(a);
   return cudaGetLastError();
 }
 
