@@ -48,6 +48,18 @@ __device__ __forceinline__ float4 lds_f32x4_sched(uint32_t addr) {
   return v;
 }
 
+// Two fp32 additions in one instruction (Blackwell's add.rn.f32x2): each half
+// is rounded to nearest-even on its own, exactly as add.rn.f32 rounds it, so
+// the packed sums are bit-identical to two __fadd_rn.
+__device__ __forceinline__ uint64_t fadd2(uint64_t acc, float x, float y) {
+  uint64_t b, r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(x), "f"(y));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(acc), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float lo_f32(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float hi_f32(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+
 __global__ void pq_lut_kernel(const float* __restrict__ books, int m, int ksub, int dsub, bool l2,
                               const float* __restrict__ queries, float* __restrict__ lut) {
   const int q = blockIdx.x;
@@ -176,7 +188,9 @@ pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
       uint32_t sw[kWords + 1];
 #pragma unroll
       for (int w = 0; w <= kWords; ++w) sw[w] = __funnelshift_rc(cw[w], cw[w + 1], shift);
-      float key[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      // Queries (0, 1) and (2, 3) of the four as packed pairs: one f32x2
+      // addition each per step.
+      uint64_t k01 = 0, k23 = 0;  // +0.0f, +0.0f
       float fin[kRows][4];
 #pragma unroll
       for (int i = 0; i < kSteps; ++i) {
@@ -184,21 +198,20 @@ pq_scan_kernel(const uint8_t* __restrict__ codes, int64_t n, int m, int ksub,
         const uint32_t c8 = __byte_perm(sw[i >> 2], 0u, 0x4404u | (static_cast<uint32_t>(i & 3) << 4));
         const float4 t = lds_f32x4_sched(off[i & (M - 1)] + c8);
         if (i >= kSkew || i >= p) {  // before step p this thread's first row has not begun
-          key[0] = __fadd_rn(key[0], t.x);
-          key[1] = __fadd_rn(key[1], t.y);
-          key[2] = __fadd_rn(key[2], t.z);
-          key[3] = __fadd_rn(key[3], t.w);
+          k01 = fadd2(k01, t.x, t.y);
+          k23 = fadd2(k23, t.z, t.w);
         }
 #pragma unroll
         for (int r = 0; r < kRows; ++r) {
           constexpr int kLast = M - 1;
           const int q = i - r * M - kLast;  // the position whose row r ends at step i
           if (q >= 0 && q <= kSkew && p == q) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              fin[r][j] = key[j];
-              key[j] = 0.0f;
-            }
+            fin[r][0] = lo_f32(k01);
+            fin[r][1] = hi_f32(k01);
+            fin[r][2] = lo_f32(k23);
+            fin[r][3] = hi_f32(k23);
+            k01 = 0;
+            k23 = 0;
           }
         }
       }
