@@ -306,6 +306,8 @@ void FlatShard::release() {
   ws.release();
   stage.release();
   segs.dev.release();
+  if (counters_h) cudaFreeHost(counters_h);
+  counters_h = nullptr;
   if (stream) cudaStreamDestroy(stream);
   stream = nullptr;
 }
@@ -580,13 +582,29 @@ static px_status shard_search(const px_flat* h, FlatShard& sh, int metric, const
   if (s != PX_OK) return s;
   cudaError_t e = sh.ws.reserve(plan.ws_bytes);
   if (e != cudaSuccess) return cuda_status(e, "search workspace allocation");
-  s = run_flat_search(h, sh, plan, metric, d_q, nq, k, d_mask, stream);
+  // The emit is enqueued before the certificate is read back, so the stream
+  // runs on without waiting for the host; the rare search with uncertified
+  // queries emits again after their fallback.
+  TensorPending pend;
+  s = run_flat_search(h, sh, plan, metric, d_q, nq, k, d_mask, stream, nullptr, &pend);
   if (s != PX_OK) return s;
   e = launch_emit(plan.final_cands, nq, k, l2, natural, sh.segs.view(h->id_offset), d_ids, d_dists,
                   stream);
   if (e != cudaSuccess) return cuda_status(e, "emit launch");
   g_launches += 1;
   sh.last_launches += 1;
+  if (pend.active) {
+    bool changed = false;
+    s = finish_flat_search(h, sh, pend, &changed);  // recounts the launches, the emit included
+    if (s != PX_OK) return s;
+    if (changed) {
+      e = launch_emit(plan.final_cands, nq, k, l2, natural, sh.segs.view(h->id_offset), d_ids, d_dists,
+                      stream);
+      if (e != cudaSuccess) return cuda_status(e, "emit launch");
+      g_launches += 1;
+      sh.last_launches += 1;
+    }
+  }
   return PX_OK;
 }
 

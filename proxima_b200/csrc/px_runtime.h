@@ -113,6 +113,7 @@ struct FlatShard {
   px::DevBuf fb;           // certificate-fallback workspace
   int64_t* out_ids = nullptr;  // results of the last search (inside stage)
   float* out_dists = nullptr;
+  int* counters_h = nullptr;   // page-locked copy of a tensor pass's device counters (4 ints)
 
   px_status ensure_capacity(int64_t need, int ld, int ldb);
   px_status append_device(const float* d_src, int64_t count, int d, int ld, int ldb, int64_t global_begin);
@@ -187,9 +188,29 @@ extern std::atomic<int> g_profiling;
 
 px_status plan_flat_search(const px_flat* h, const FlatShard& sh, int64_t nq, int k, bool masked,
                            SearchPlan& plan);
+// A tensor-core search whose certificate has not been read back yet: its
+// candidates are in plan.final_cands, provisionally (every query certified).
+struct TensorPending {
+  bool active = false;
+  int metric = 0, k = 0, first = 0;
+  int64_t nq = 0, launches0 = 0;
+  const float* d_q = nullptr;
+  const uint8_t* d_mask = nullptr;
+  const uint32_t* mask_bits = nullptr;
+  int* fail_list = nullptr;
+  uint64_t* final_cands = nullptr;
+  cudaStream_t stream = nullptr;
+};
+// With pend == nullptr the search completes before it returns. Otherwise a
+// tensor-core search returns after enqueueing its rescoring and the copy of
+// its certificate counters (pend->active): the caller may enqueue work on
+// the candidates (the emit), then must call finish_flat_search, which waits
+// for the stream and runs the refinement or the exact scan for uncertified
+// queries; *changed then says whether the candidates were rewritten.
 px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int metric,
                           const float* d_q, int64_t nq, int k, const uint8_t* d_mask,
-                          cudaStream_t stream, void* ws = nullptr);
+                          cudaStream_t stream, void* ws = nullptr, TensorPending* pend = nullptr);
+px_status finish_flat_search(const px_flat* h, FlatShard& sh, TensorPending& pend, bool* changed);
 px_status first_pass_candidates(const px_flat* h, FlatShard& sh, int metric, const float* d_q, int64_t nq,
                                 int k, cudaStream_t stream, const uint64_t** merged, int* cands, int* pass);
 

@@ -266,13 +266,12 @@ static px_status exact_for_list(const px_flat* h, FlatShard& sh, int metric, con
 // One tensor-core candidate pass: convert the queries, K1 over the shard
 // (bf16 copies, tf32 hi values, or the three-pass tf32 sum), split merge,
 // exact rescoring and certificate. Leaves exact candidates in w.final_cands
-// and the uncertified queries in w.fail_list; reads back their count and
-// whether the pass's operands were inexact, i.e. whether a more precise pass
-// could certify them (the one host wait of the pass).
-static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& plan, int metric,
-                             const float* d_q, int64_t nq, int k, const uint32_t* mask_bits, PassKind kind,
-                             const TensorWs& w, bool profile_main, cudaStream_t stream, int* n_fail,
-                             bool* inexact) {
+// and the uncertified queries in w.fail_list, and enqueues the copy of the
+// pass's counters to the shard's page-locked sh.counters_h (read by
+// tensor_pass_read once the stream has reached it).
+static px_status tensor_pass_launch(const px_flat* h, FlatShard& sh, const SearchPlan& plan, int metric,
+                                    const float* d_q, int64_t nq, int k, const uint32_t* mask_bits,
+                                    PassKind kind, const TensorWs& w, bool profile_main, cudaStream_t stream) {
   const bool l2 = metric == PX_METRIC_L2;
   // An L2 bf16 pass over rows that carry their norms in the padding runs as
   // an inner product of 2q with them: no per-element norm term in the
@@ -361,10 +360,23 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
   e = launch_rescore(r, stream);
   if (e != cudaSuccess) return cuda_status(e, "rescore launch");
   g_launches += 5;  // split, gemm, merge, rescore (+ memset counted as one)
-  int hc[4] = {0, 0, 0, 0};
-  e = cudaMemcpyAsync(hc, w.counters, sizeof(hc), cudaMemcpyDeviceToHost, stream);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (sh.counters_h == nullptr) {
+    e = cudaMallocHost(&sh.counters_h, sizeof(int) * 4);
+    if (e != cudaSuccess) {
+      sh.counters_h = nullptr;
+      return cuda_status(e, "certificate readback buffer");
+    }
+  }
+  e = cudaMemcpyAsync(sh.counters_h, w.counters, sizeof(int) * 4, cudaMemcpyDeviceToHost, stream);
   if (e != cudaSuccess) return cuda_status(e, "certificate readback");
+  return PX_OK;
+}
+
+// After the stream has passed a tensor pass's counter copy: the count of
+// uncertified queries, and whether the pass's operands were inexact, i.e.
+// whether a more precise pass could certify them.
+static px_status tensor_pass_read(const FlatShard& sh, PassKind kind, int* n_fail, bool* inexact) {
+  const int* hc = sh.counters_h;
   if (hc[2] != 0)
     return set_error(PX_ETIMEOUT, "a tensor-core pipeline wait timed out on device " +
                                       std::to_string(sh.device) + "; the search was abandoned");
@@ -373,9 +385,83 @@ static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& 
   return PX_OK;
 }
 
+// The whole pass with its one host wait.
+static px_status tensor_pass(const px_flat* h, FlatShard& sh, const SearchPlan& plan, int metric,
+                             const float* d_q, int64_t nq, int k, const uint32_t* mask_bits, PassKind kind,
+                             const TensorWs& w, bool profile_main, cudaStream_t stream, int* n_fail,
+                             bool* inexact) {
+  px_status s = tensor_pass_launch(h, sh, plan, metric, d_q, nq, k, mask_bits, kind, w, profile_main, stream);
+  if (s != PX_OK) return s;
+  cudaError_t e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_status(e, "certificate readback");
+  return tensor_pass_read(sh, kind, n_fail, inexact);
+}
+
+// Refinement or exact scan for the queries a first tensor pass left
+// uncertified (n_fail of them, listed in fail_list); their exact candidates
+// are scattered into final_cands.
+static px_status certify_rest(const px_flat* h, FlatShard& sh, int metric, const float* d_q, int k,
+                              const uint8_t* d_mask, const uint32_t* mask_bits, PassKind first, int n_fail,
+                              bool inexact, int* fail_list, uint64_t* final_cands, cudaStream_t stream) {
+  if (first != kPass3xTf32 && inexact && refine_pays(n_fail, k)) {
+    SearchPlan p2;
+    plan_gemm(sh, n_fail, k, kPass3xTf32, h->sample_mode, p2);
+    Carver c2;
+    c2.take(sizeof(float) * static_cast<size_t>(n_fail) * h->dim);
+    TensorWs w2;
+    carve_tensor_ws(c2, p2, n_fail, h->ld, h->ldb, k, kPass3xTf32, w2);
+    cudaError_t e = sh.ws2.reserve(c2.used);
+    if (e != cudaSuccess) return cuda_status(e, "refinement workspace allocation");
+    c2 = Carver(sh.ws2.ptr);
+    float* fq = static_cast<float*>(c2.take(sizeof(float) * static_cast<size_t>(n_fail) * h->dim));
+    carve_tensor_ws(c2, p2, n_fail, h->ld, h->ldb, k, kPass3xTf32, w2);
+    e = launch_gather_rows(d_q, h->dim, fail_list, n_fail, fq, stream);
+    if (e != cudaSuccess) return cuda_status(e, "refinement gather");
+    int n_fail2 = 0;
+    bool inexact2 = false;
+    px_status s = tensor_pass(h, sh, p2, metric, fq, n_fail, k, mask_bits, kPass3xTf32, w2, false, stream,
+                              &n_fail2, &inexact2);
+    if (s != PX_OK) return s;
+    if (n_fail2 > 0) {
+      s = exact_for_list(h, sh, metric, fq, w2.fail_list, n_fail2, k, d_mask, w2.final_cands, stream);
+      if (s != PX_OK) return s;
+    }
+    e = launch_scatter_cands(w2.final_cands, k, fail_list, n_fail, final_cands, stream);
+    if (e != cudaSuccess) return cuda_status(e, "refinement scatter");
+    g_launches += 2;
+    sh.last_refined = n_fail;
+    sh.last_fallback = n_fail2;
+    return PX_OK;
+  }
+  px_status s = exact_for_list(h, sh, metric, d_q, fail_list, n_fail, k, d_mask, final_cands, stream);
+  if (s != PX_OK) return s;
+  sh.last_fallback = n_fail;
+  return PX_OK;
+}
+
+px_status finish_flat_search(const px_flat* h, FlatShard& sh, TensorPending& pend, bool* changed) {
+  *changed = false;
+  pend.active = false;
+  cudaError_t e = cudaStreamSynchronize(pend.stream);
+  if (e != cudaSuccess) return cuda_status(e, "certificate readback");
+  int n_fail = 0;
+  bool inexact = false;
+  const PassKind first = static_cast<PassKind>(pend.first);
+  px_status s = tensor_pass_read(sh, first, &n_fail, &inexact);
+  if (s != PX_OK) return s;
+  if (n_fail > 0) {
+    s = certify_rest(h, sh, pend.metric, pend.d_q, pend.k, pend.d_mask, pend.mask_bits, first, n_fail, inexact,
+                     pend.fail_list, pend.final_cands, pend.stream);
+    if (s != PX_OK) return s;
+    *changed = true;
+  }
+  sh.last_launches = static_cast<int>(g_launches.load() - pend.launches0);
+  return PX_OK;
+}
+
 px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int metric,
                           const float* d_q, int64_t nq, int k, const uint8_t* d_mask,
-                          cudaStream_t stream, void* ws) {
+                          cudaStream_t stream, void* ws, TensorPending* pend) {
   const bool prof = g_profiling.load() != 0;
   sh.last_path = static_cast<int>(plan.path);
   sh.last_fallback = 0;
@@ -412,47 +498,26 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
     cudaError_t e = launch_pack_mask(d_mask, sh.n, mask_bits, stream);
     if (e != cudaSuccess) return cuda_status(e, "mask pack");
   }
-  int n_fail = 0;
-  bool inexact = false;
-  px_status s = tensor_pass(h, sh, plan, metric, d_q, nq, k, mask_bits, first, w, prof, stream, &n_fail, &inexact);
+  px_status s = tensor_pass_launch(h, sh, plan, metric, d_q, nq, k, mask_bits, first, w, prof, stream);
   if (s != PX_OK) return s;
-  if (n_fail > 0) {
-    if (first != kPass3xTf32 && inexact && refine_pays(n_fail, k)) {
-      SearchPlan p2;
-      plan_gemm(sh, n_fail, k, kPass3xTf32, h->sample_mode, p2);
-      Carver c2;
-      c2.take(sizeof(float) * static_cast<size_t>(n_fail) * h->dim);
-      TensorWs w2;
-      carve_tensor_ws(c2, p2, n_fail, h->ld, h->ldb, k, kPass3xTf32, w2);
-      cudaError_t e = sh.ws2.reserve(c2.used);
-      if (e != cudaSuccess) return cuda_status(e, "refinement workspace allocation");
-      c2 = Carver(sh.ws2.ptr);
-      float* fq = static_cast<float*>(c2.take(sizeof(float) * static_cast<size_t>(n_fail) * h->dim));
-      carve_tensor_ws(c2, p2, n_fail, h->ld, h->ldb, k, kPass3xTf32, w2);
-      e = launch_gather_rows(d_q, h->dim, w.fail_list, n_fail, fq, stream);
-      if (e != cudaSuccess) return cuda_status(e, "refinement gather");
-      int n_fail2 = 0;
-      bool inexact2 = false;
-      s = tensor_pass(h, sh, p2, metric, fq, n_fail, k, mask_bits, kPass3xTf32, w2, false, stream, &n_fail2,
-                      &inexact2);
-      if (s != PX_OK) return s;
-      if (n_fail2 > 0) {
-        s = exact_for_list(h, sh, metric, fq, w2.fail_list, n_fail2, k, d_mask, w2.final_cands, stream);
-        if (s != PX_OK) return s;
-      }
-      e = launch_scatter_cands(w2.final_cands, k, w.fail_list, n_fail, w.final_cands, stream);
-      if (e != cudaSuccess) return cuda_status(e, "refinement scatter");
-      g_launches += 2;
-      sh.last_refined = n_fail;
-      sh.last_fallback = n_fail2;
-    } else {
-      s = exact_for_list(h, sh, metric, d_q, w.fail_list, n_fail, k, d_mask, w.final_cands, stream);
-      if (s != PX_OK) return s;
-      sh.last_fallback = n_fail;
-    }
-  }
+  TensorPending local;
+  TensorPending& p = pend ? *pend : local;
+  p.active = true;
+  p.metric = metric;
+  p.k = k;
+  p.first = first;
+  p.nq = nq;
+  p.launches0 = launches0;
+  p.d_q = d_q;
+  p.d_mask = d_mask;
+  p.mask_bits = mask_bits;
+  p.fail_list = w.fail_list;
+  p.final_cands = w.final_cands;
+  p.stream = stream;
   sh.last_launches = static_cast<int>(g_launches.load() - launches0);
-  return PX_OK;
+  if (pend) return PX_OK;
+  bool changed = false;
+  return finish_flat_search(h, sh, p, &changed);
 }
 
 // Instrumentation: the first tensor-core candidate pass alone (query
