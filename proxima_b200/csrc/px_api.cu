@@ -106,8 +106,9 @@ void HostBuf::release() {
 
 // A float is NaN or infinite exactly when its exponent bits are all ones.
 // The loop has no early exit, so the compiler vectorizes it; inputs of more
-// than 4M values are split over host threads (config 4's 10k queries are
-// 7.7M values, a host add can be billions).
+// than 2M values are split over host threads, at least 1M values each
+// (config 4's 10k queries are 7.7M values, 1.9 ms on one core and 0.45 ms on
+// seven; a host add can be billions).
 static bool finite_range(const float* p, size_t count) {
   const uint32_t* u = reinterpret_cast<const uint32_t*>(p);
   uint32_t bad = 0;
@@ -119,7 +120,7 @@ bool all_finite(const float* p, int64_t count) {
   if (count <= 0) return true;
   const size_t n = static_cast<size_t>(count);
   const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-  const size_t threads = std::min<size_t>(std::min<size_t>(hw, 32), n / (size_t(1) << 22));
+  const size_t threads = std::min<size_t>(std::min<size_t>(hw, 32), n / (size_t(1) << 20));
   if (threads <= 1) return finite_range(p, n);
   std::vector<char> ok(threads, 1);
   std::vector<std::thread> pool;
