@@ -487,7 +487,7 @@ def run_ours(args, cfg, rank, world, local_rank):
 
     # ---- device-resident timing with kernel profiling -------------------
     _lib.set_profiling(True)
-    kernel_ms, fallbacks, refined = [], 0, 0
+    index.local.profile_totals(reset=True)
     launches0 = _lib.launch_count()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
@@ -495,14 +495,14 @@ def run_ours(args, cfg, rank, world, local_rank):
         start.record()
         for _ in range(args.steps):
             step_device()
-            prof = index.local.last_search_profile()
-            if prof["main_kernel_ms"] is not None:
-                kernel_ms.append(prof["main_kernel_ms"])
-            fallbacks += prof["fallback_queries"]
-            refined += prof["refined_queries"]
         stop.record()
         barrier()
     launches = _lib.launch_count() - launches0
+    # The library sums the dominant kernel's event times over the timed
+    # searches, so the loop above reads nothing back between steps.
+    tot = index.local.profile_totals()
+    kernel_ms = [tot["main_kernel_ms"] / tot["profiled_searches"]] if tot["profiled_searches"] else []
+    fallbacks, refined = tot["fallback_queries"], tot["refined_queries"]
     _lib.set_profiling(False)
     dev_ms = start.elapsed_time(stop)
     t = torch.tensor([dev_ms], dtype=torch.float64, device=device)

@@ -140,6 +140,16 @@ typedef struct px_search_profile {
 } px_search_profile;
 PX_API void px_set_profiling(int32_t enable);
 PX_API px_status px_flat_last_profile(const px_flat* h, px_search_profile* out);
+/* Totals over the handle's searches (first shard) since the last reset, so a
+ * benchmark loop need not read the profile after every search. */
+typedef struct px_profile_totals {
+  double main_kernel_ms;      /* summed device time of the profiled searches' dominant kernel */
+  int64_t profiled_searches;  /* searches with profiling on */
+  int64_t searches;
+  int64_t fallback_queries;
+  int64_t refined_queries;
+} px_profile_totals;
+PX_API px_status px_flat_profile_totals(px_flat* h, int32_t reset, px_profile_totals* out);
 /* Total kernels launched by this library in this process. */
 PX_API int64_t px_launch_count(void);
 

@@ -242,6 +242,17 @@ class FlatIndex:
         way; this only changes speed."""
         _lib.check(self._lib.px_flat_set_sample_pass(self._h, self._SAMPLE[mode]))
 
+    def profile_totals(self, reset: bool = False) -> dict:
+        """Totals over this index's searches since the last reset: the summed
+        device time of the profiled searches' dominant kernel, their count,
+        all searches, and the queries sent to the refinement and the exact
+        scan. reset=True zeroes them after reading."""
+        t = _lib.ProfileTotals()
+        _lib.check(self._lib.px_flat_profile_totals(self._h, 1 if reset else 0, ctypes.byref(t)))
+        return {"main_kernel_ms": t.main_kernel_ms, "profiled_searches": t.profiled_searches,
+                "searches": t.searches, "fallback_queries": t.fallback_queries,
+                "refined_queries": t.refined_queries}
+
     def last_search_profile(self) -> dict:
         """Path, kernel launches, queries the certificate sent to the
         three-pass refinement and to the exact scan, and (when profiling is

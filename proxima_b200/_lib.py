@@ -41,6 +41,13 @@ _i32p = _c.POINTER(_c.c_int32)
 _u8p = _c.POINTER(_c.c_uint8)
 _llp = _c.POINTER(_c.c_longlong)
 
+class ProfileTotals(ctypes.Structure):
+    """px_profile_totals (include/px.h)."""
+    _fields_ = [("main_kernel_ms", ctypes.c_double), ("profiled_searches", ctypes.c_int64),
+                ("searches", ctypes.c_int64), ("fallback_queries", ctypes.c_int64),
+                ("refined_queries", ctypes.c_int64)]
+
+
 class SearchProfile(ctypes.Structure):
     """px_search_profile (include/px.h)."""
     _fields_ = [("path", ctypes.c_int32), ("launches", ctypes.c_int32),
@@ -71,6 +78,7 @@ SIGNATURES = {
     "px_flat_set_sample_pass": (_i32, [_vp, _i32]),
     "px_set_profiling": (None, [_i32]),
     "px_flat_last_profile": (_i32, [_vp, _vp]),
+    "px_flat_profile_totals": (_i32, [_vp, _i32, _vp]),
     "px_launch_count": (_i64, []),
     "px_flat_search": (_i32, [_vp, _f32p, _i64, _i32, _i64p, _f32p]),
     "px_flat_search_filtered": (_i32, [_vp, _f32p, _i64, _i32, _u8p, _i64p, _f32p]),

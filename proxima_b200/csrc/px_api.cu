@@ -445,6 +445,26 @@ PX_API void px_set_profiling(int32_t enable) { g_profiling = enable ? 1 : 0; }
 
 PX_API int64_t px_launch_count(void) { return g_launches.load(); }
 
+PX_API px_status px_flat_profile_totals(px_flat* h, int32_t reset, px_profile_totals* out) {
+  px_status s = flat_check(h);
+  if (s != PX_OK) return s;
+  if (out == nullptr) return set_error(PX_EINVAL, "out is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  FlatShard& sh = h->shards[0];
+  s = flush_search_profile(sh);
+  if (s != PX_OK) return s;
+  out->main_kernel_ms = sh.tot_ms;
+  out->profiled_searches = sh.tot_profiled;
+  out->searches = sh.tot_searches;
+  out->fallback_queries = sh.tot_fallback;
+  out->refined_queries = sh.tot_refined;
+  if (reset) {
+    sh.tot_ms = 0.0;
+    sh.tot_profiled = sh.tot_searches = sh.tot_fallback = sh.tot_refined = 0;
+  }
+  return PX_OK;
+}
+
 PX_API px_status px_flat_last_profile(const px_flat* h, px_search_profile* out) {
   px_status s = flat_check(h);
   if (s != PX_OK) return s;
@@ -570,6 +590,15 @@ PX_API px_status px_flat_add_device(px_flat* h, const float* d_rows, int64_t n) 
 
 }  // extern "C"
 
+// A search of this shard has been enqueued in full: its counts go to the
+// totals now, its kernel time (if profiled) when flush_search_profile runs.
+static void note_search_done(FlatShard& sh) {
+  sh.tot_searches += 1;
+  sh.tot_fallback += sh.last_fallback;
+  sh.tot_refined += sh.last_refined;
+  if (sh.last_profiled) sh.prof_pending = true;  // an unprofiled search records no events
+}
+
 // Runs one shard's search on its device. d_q: nq x dim on the shard's device.
 // Writes nq x k ids (global) and distances (natural or key space).
 static px_status shard_search(const px_flat* h, FlatShard& sh, int metric, const float* d_q,
@@ -606,6 +635,7 @@ static px_status shard_search(const px_flat* h, FlatShard& sh, int metric, const
       sh.last_launches += 1;
     }
   }
+  note_search_done(sh);
   return PX_OK;
 }
 
@@ -641,6 +671,11 @@ static px_status flat_search_replay(px_flat* h, FlatShard& sh, const SearchPlan&
                                     const float* queries, int64_t nq, int32_t k, bool natural, int64_t* out_ids,
                                     float* out_dists, bool* captured) {
   *captured = true;
+  // A graph captured with profiling on records the profiling events when it
+  // is replayed: take the last profiled search's time first (and never wait
+  // on an event inside the capture below).
+  px_status fs = flush_search_profile(sh);
+  if (fs != PX_OK) return fs;
   SearchPlan plan = plan_in;
   const size_t qbytes = sizeof(float) * static_cast<size_t>(nq) * h->dim;
   const size_t obytes = static_cast<size_t>(nq) * k;
@@ -738,6 +773,7 @@ static px_status flat_search_replay(px_flat* h, FlatShard& sh, const SearchPlan&
   sh.last_sample_tiles = 0;
   sh.last_launches = 3;
   sh.last_profiled = false;
+  note_search_done(sh);
   std::memcpy(out_ids, pin + q_al, obytes * sizeof(int64_t));
   std::memcpy(out_dists, pin + q_al + obytes * sizeof(int64_t), obytes * sizeof(float));
   return PX_OK;

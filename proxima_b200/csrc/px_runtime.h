@@ -114,6 +114,11 @@ struct FlatShard {
   int64_t* out_ids = nullptr;  // results of the last search (inside stage)
   float* out_dists = nullptr;
   int* counters_h = nullptr;   // page-locked copy of a tensor pass's device counters (4 ints)
+  // Totals since the last px_flat_profile_totals reset; the last profiled
+  // search's kernel time is added when the events are next needed.
+  bool prof_pending = false;
+  double tot_ms = 0.0;
+  int64_t tot_profiled = 0, tot_searches = 0, tot_fallback = 0, tot_refined = 0;
 
   px_status ensure_capacity(int64_t need, int ld, int ldb);
   px_status append_device(const float* d_src, int64_t count, int d, int ld, int ldb, int64_t global_begin);
@@ -211,6 +216,9 @@ px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int
                           const float* d_q, int64_t nq, int k, const uint8_t* d_mask,
                           cudaStream_t stream, void* ws = nullptr, TensorPending* pend = nullptr);
 px_status finish_flat_search(const px_flat* h, FlatShard& sh, TensorPending& pend, bool* changed);
+// Adds the last profiled search's kernel time to the shard's totals (waits
+// for its stop event); called before the events are recorded again.
+px_status flush_search_profile(FlatShard& sh);
 px_status first_pass_candidates(const px_flat* h, FlatShard& sh, int metric, const float* d_q, int64_t nq,
                                 int k, cudaStream_t stream, const uint64_t** merged, int* cands, int* pass);
 

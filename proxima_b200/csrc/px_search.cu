@@ -439,6 +439,19 @@ static px_status certify_rest(const px_flat* h, FlatShard& sh, int metric, const
   return PX_OK;
 }
 
+px_status flush_search_profile(FlatShard& sh) {
+  if (!sh.prof_pending) return PX_OK;
+  sh.prof_pending = false;
+  DeviceGuard dg(sh.device);
+  float ms = 0.f;
+  cudaError_t e = cudaEventSynchronize(sh.ev_stop);
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, sh.ev_start, sh.ev_stop);
+  if (e != cudaSuccess) return cuda_status(e, "profile events");
+  sh.tot_ms += ms;
+  sh.tot_profiled += 1;
+  return PX_OK;
+}
+
 px_status finish_flat_search(const px_flat* h, FlatShard& sh, TensorPending& pend, bool* changed) {
   *changed = false;
   pend.active = false;
@@ -462,6 +475,8 @@ px_status finish_flat_search(const px_flat* h, FlatShard& sh, TensorPending& pen
 px_status run_flat_search(const px_flat* h, FlatShard& sh, SearchPlan& plan, int metric,
                           const float* d_q, int64_t nq, int k, const uint8_t* d_mask,
                           cudaStream_t stream, void* ws, TensorPending* pend) {
+  px_status fs = flush_search_profile(sh);
+  if (fs != PX_OK) return fs;
   const bool prof = g_profiling.load() != 0;
   sh.last_path = static_cast<int>(plan.path);
   sh.last_fallback = 0;

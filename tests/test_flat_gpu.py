@@ -580,3 +580,34 @@ def test_tensor_path_sample_pass_ties(pxm):
     ids, d, prof = _run_sampled(pxm, data, O.IP, queries, 10)
     assert prof["sample_tiles"] == 32, prof
     _parity.check_flat(data, O.IP, queries, ids, d, 10)
+
+
+def test_profile_totals(pxm):
+    # The totals a benchmark reads once after its loop: every search counted,
+    # the profiled ones' kernel times summed, and a reset.
+    data = _data.unit_gaussian(20000, 64, 81)
+    queries = _data.unit_gaussian(64, 64, 82)
+    idx = pxm.FlatIndex(64, pxm.Metric.InnerProduct)
+    idx.add(data)
+    idx.set_search_path("tensor")
+    idx.search_batch(queries, k=10)
+    idx.profile_totals(reset=True)
+    pxm.set_profiling(True)
+    try:
+        times = []
+        for _ in range(3):
+            idx.search_batch(queries, k=10)
+            times.append(idx.last_search_profile()["main_kernel_ms"])
+        idx.set_search_path("exact")
+        idx.search(queries[0], k=10)  # a small exact batch: profiled unless it replays a graph
+        last = idx.last_search_profile()["main_kernel_ms"]
+        if last is not None:
+            times.append(last)
+    finally:
+        pxm.set_profiling(False)
+    t = idx.profile_totals()
+    assert t["searches"] == 4 and t["profiled_searches"] == len(times), (t, times)
+    assert abs(t["main_kernel_ms"] - sum(times)) <= 1e-3 * sum(times) + 1e-6, (t, times)
+    assert t["fallback_queries"] == 0 and t["refined_queries"] == 0
+    assert idx.profile_totals(reset=True)["searches"] == 4
+    assert idx.profile_totals()["searches"] == 0
