@@ -611,3 +611,32 @@ def test_profile_totals(pxm):
     assert t["fallback_queries"] == 0 and t["refined_queries"] == 0
     assert idx.profile_totals(reset=True)["searches"] == 4
     assert idx.profile_totals()["searches"] == 0
+
+
+def test_tensor_path_repeated_searches(pxm):
+    # Repeated tensor-core searches reuse the handle's workspace and staging:
+    # new query values, another k, an add (the rows move) and certificate
+    # fallbacks on every repeat all stay exact.
+    data = _data.unit_gaussian(24000, 64, 91)
+    idx = pxm.FlatIndex(64, pxm.Metric.InnerProduct)
+    idx.add(data[:18000])
+    idx.set_search_path("tensor")
+    for seed in (92, 93, 94):
+        queries = _data.unit_gaussian(64, 64, seed)
+        ids, d = idx.search_batch(queries, k=10)
+        assert idx.last_search_profile()["path"] == "tensor"
+        _parity.check_flat(data[:18000], O.IP, queries, ids, d, 10)
+    ids, d = idx.search_batch(queries, k=16)
+    _parity.check_flat(data[:18000], O.IP, queries, ids, d, 16)
+    idx.add(data[18000:])
+    ids, d = idx.search_batch(queries, k=10)
+    _parity.check_flat(data, O.IP, queries, ids, d, 10)
+    # Certificate fallbacks still run after a replay: duplicated rows defeat it.
+    dup = np.repeat(data[:400], 40, axis=0)
+    idx2 = pxm.FlatIndex(64, pxm.Metric.InnerProduct)
+    idx2.add(dup)
+    idx2.set_search_path("tensor")
+    for _ in range(2):
+        ids, d = idx2.search_batch(queries[:32], k=10)
+        assert idx2.last_search_profile()["fallback_queries"] > 0
+        _parity.check_flat(dup, O.IP, queries[:32], ids, d, 10)
