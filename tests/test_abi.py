@@ -130,3 +130,6 @@ def test_record_layout_and_new_entry_points_validate_without_gpu(px):
                                         ctypes.byref(kind)) == px._lib.PX_EINVAL
     assert lib.px_pq_search_device(None, None, 1, 10, 0, None, None, None) == px._lib.PX_EINVAL
     assert lib.px_flat_set_sample_pass(None, 0) == px._lib.PX_EINVAL
+    totals = px._lib.ProfileTotals()
+    assert lib.px_flat_profile_totals(None, 0, ctypes.byref(totals)) == px._lib.PX_EINVAL
+    assert ctypes.sizeof(px._lib.ProfileTotals) == 40  # double + 4 x int64, as in px.h
