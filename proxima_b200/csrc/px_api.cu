@@ -109,11 +109,31 @@ void HostBuf::release() {
 // than 2M values are split over host threads, at least 1M values each
 // (config 4's 10k queries are 7.7M values, 1.9 ms on one core and 0.45 ms on
 // seven; a host add can be billions).
-static bool finite_range(const float* p, size_t count) {
+// The same loop built for AVX2 (eight values per compare) runs at about twice
+// the rate of the baseline-x86-64 build (config 1's 384k query values: 62
+// against 121 us); it is used only where the CPU reports AVX2.
+static bool finite_range_portable(const float* p, size_t count) {
   const uint32_t* u = reinterpret_cast<const uint32_t*>(p);
   uint32_t bad = 0;
   for (size_t i = 0; i < count; ++i) bad |= (u[i] & 0x7f800000u) == 0x7f800000u ? 1u : 0u;
   return bad == 0;
+}
+
+#if defined(__x86_64__)
+__attribute__((target("avx2"))) static bool finite_range_avx2(const float* p, size_t count) {
+  const uint32_t* u = reinterpret_cast<const uint32_t*>(p);
+  uint32_t bad = 0;
+  for (size_t i = 0; i < count; ++i) bad |= (u[i] & 0x7f800000u) == 0x7f800000u ? 1u : 0u;
+  return bad == 0;
+}
+#endif
+
+static bool finite_range(const float* p, size_t count) {
+#if defined(__x86_64__)
+  static const bool avx2 = __builtin_cpu_supports("avx2");
+  if (avx2) return finite_range_avx2(p, count);
+#endif
+  return finite_range_portable(p, count);
 }
 
 bool all_finite(const float* p, int64_t count) {

@@ -133,3 +133,28 @@ def test_record_layout_and_new_entry_points_validate_without_gpu(px):
     totals = px._lib.ProfileTotals()
     assert lib.px_flat_profile_totals(None, 0, ctypes.byref(totals)) == px._lib.PX_EINVAL
     assert ctypes.sizeof(px._lib.ProfileTotals) == 40  # double + 4 x int64, as in px.h
+
+
+def test_non_finite_inputs_are_rejected_without_gpu(px):
+    """The host finiteness check (vectorized, and split over threads for long
+    inputs) on every length class and position: px_pq_train runs it before it
+    needs a device, so a rejected input reports EINVAL and an accepted one
+    gets as far as the missing device."""
+    lib = px._lib.load()
+    if lib.px_device_count() > 0:
+        pytest.skip("a GPU is present (the accepted case would train)")
+    books = np.zeros(2 * 2 * 2, dtype=np.float32)  # m=2 subspaces x 2 centroids x dsub 2
+    bad_bits = [0x7fc00000, 0xffc00000, 0x7f800000, 0xff800000, 0x7f800001]
+    for count in (8, 12, 36, 4000, 2_400_000):
+        base = np.full(count, 1.5, dtype=np.float32)
+        base[count // 3] = np.float32(3.4028235e38)  # FLT_MAX is finite
+        for pos in sorted({0, 1, 7, count // 2, count - 1}):
+            for bits in bad_bits:
+                x = base.copy()
+                x.view(np.uint32)[pos] = bits
+                st = lib.px_pq_train(x.ctypes.data_as(px._lib._f32p), count // 4, 4, 2, 1, 1, 0, 1, 0,
+                                     books.ctypes.data_as(px._lib._f32p))
+                assert st == px._lib.PX_EINVAL and "NaN or infinite" in px._lib.last_error(), (count, pos, hex(bits))
+        st = lib.px_pq_train(base.ctypes.data_as(px._lib._f32p), count // 4, 4, 2, 1, 1, 0, 1, 0,
+                             books.ctypes.data_as(px._lib._f32p))
+        assert st != px._lib.PX_EINVAL, (count, px._lib.last_error())
